@@ -1,0 +1,169 @@
+/*
+ * bfft.h -- C ABI of the B200 FFT library (libbfft.so).
+ *
+ * The drop-in boundary for the reference's plan/operator API
+ * (src/xpu/entry.py:292 plan_fft, :501 execute_fft_plan, src/xpu/runner.py
+ * runner functions).  The reference has no C ABI of its own
+ * (docs/reference/api.md:40): its Python layer calls Triton kernels directly.
+ * Here the Python host layer (kunlunxin-fft_b200/bfft) resolves a plan on the
+ * host exactly like the reference and then calls these entry points with
+ * plain device pointers, sizes and a CUDA stream; an FFI from any other host
+ * language would bind the same symbols.
+ *
+ * Conventions
+ *   - Data is interleaved complex64 (float re, float im), batch-major (B, N),
+ *     contiguous; R2C input / C2R output are float32 (B, N).
+ *   - All pointers are device pointers on the plan's device; `stream` is a
+ *     cudaStream_t (NULL = legacy default stream).  Nothing synchronises the
+ *     host: calls enqueue work on `stream` and return.
+ *   - Every entry point returns a bfft_status; 0 is success.  On failure
+ *     bfft_last_error() returns a thread-local message.  Shape / value errors
+ *     are detected before any launch.
+ *   - Input and output must not overlap.
+ */
+#ifndef BFFT_H
+#define BFFT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BFFT_API_VERSION 1
+
+#if defined(__GNUC__)
+#define BFFT_EXPORT __attribute__((visibility("default")))
+#else
+#define BFFT_EXPORT
+#endif
+
+typedef enum bfft_status {
+    BFFT_OK = 0,
+    BFFT_ERR_VALUE = 1,       /* bad enum / parameter (-> ValueError)            */
+    BFFT_ERR_SHAPE = 2,       /* N / batch / shape contract (-> ValueError)      */
+    BFFT_ERR_UNSUPPORTED = 3, /* no lowering for this combination (-> ValueError)*/
+    BFFT_ERR_CUDA = 4,        /* CUDA runtime failure (-> RuntimeError)          */
+    BFFT_ERR_NCCL = 5,        /* NCCL failure in a distributed plan              */
+    BFFT_ERR_ALLOC = 6,       /* device allocation failed (-> MemoryError)       */
+    BFFT_ERR_WORKSPACE = 7    /* workspace missing or too small (-> ValueError)  */
+} bfft_status;
+
+/* Decomposition direction (the reference's `direction`, entry.py:68). */
+enum { BFFT_DIT = 0, BFFT_DIF = 1 };
+/* transform_type (config.py:34). */
+enum { BFFT_C2C = 0, BFFT_R2C = 1, BFFT_C2R = 2 };
+/* transform_direction (config.py:35). */
+enum { BFFT_FORWARD = 0, BFFT_INVERSE = 1 };
+/* norm (config.py:36, entry.py:81-102). */
+enum { BFFT_NORM_NONE = 0, BFFT_NORM_FORWARD = 1, BFFT_NORM_BACKWARD = 2, BFFT_NORM_ORTHO = 3 };
+/* Batch variant of the M4 stage flow (runner.py:781-841). */
+enum { BFFT_SPREAD = 0, BFFT_FOLDED = 1 };
+/* Real-transform flow (entry.py:555-616): compat = packed C2C, dedicated =
+ * half-length core + stitch / pre-twiddle / unpack epilogues. */
+enum { BFFT_REAL_COMPAT = 0, BFFT_REAL_DEDICATED = 1 };
+
+/* Runner identities: the reference's `plan.executed` names
+ * (entry.py:175-225, runner.py, adapter_hybrid.py:224). */
+typedef enum bfft_runner {
+    BFFT_RUN_FFT_DIT = 0,              /* runner.py:118  M0 radix-2 DIT           */
+    BFFT_RUN_FFT_DIF = 1,              /* runner.py:166  M0 radix-2 DIF           */
+    BFFT_RUN_FFT_DIT_BATCH = 2,        /* runner.py:781  M4 batched DIT           */
+    BFFT_RUN_FFT_DIF_BATCH = 3,        /* runner.py:844  M4 batched DIF           */
+    BFFT_RUN_FFT_DIT_RADIX4 = 4,       /* runner.py:1399 M5 radix-4 DIT           */
+    BFFT_RUN_FFT_DIF_RADIX4 = 5,       /* runner.py:1472 M5 radix-4 DIF           */
+    BFFT_RUN_FFT_DIT_RADIX4_BATCH = 6, /* runner.py:1112                          */
+    BFFT_RUN_FFT_DIF_RADIX4_BATCH = 7, /* runner.py:1193                          */
+    BFFT_RUN_FFT_DIT_FUSED = 8,        /* runner.py:209  M1 fused local tile      */
+    BFFT_RUN_FFT_DIT_MATRIX = 9,       /* runner.py:379  M2 local group + tail    */
+    BFFT_RUN_FFT_DIF_MATRIX = 10,      /* runner.py:445                           */
+    BFFT_RUN_FFT_DIT_MATRIX_BATCH = 11,/* runner.py:956  batch local-fused core   */
+    BFFT_RUN_FFT_DIF_MATRIX_BATCH = 12,/* runner.py:1038                          */
+    BFFT_RUN_FFT_DIT_GROUPED = 13,     /* runner.py:603  M3 grouped tail          */
+    BFFT_RUN_FFT_DIF_GROUPED = 14,     /* runner.py:685                           */
+    BFFT_RUN_RUN_HYBRID = 15           /* adapter_hybrid.py:224 4-step (N = T*R)  */
+} bfft_runner;
+
+/* Everything a plan needs; mirrors the fields of the reference's
+ * ExecutionPlan (entry.py:105-125) that affect execution. */
+typedef struct bfft_plan_desc {
+    int32_t runner;              /* bfft_runner                                   */
+    int32_t direction;           /* BFFT_DIT / BFFT_DIF                           */
+    int64_t n;                   /* transform length (full length for R2C / C2R)  */
+    int64_t batch;               /* number of transforms (>= 1)                   */
+    int32_t transform_type;      /* BFFT_C2C / BFFT_R2C / BFFT_C2R                */
+    int32_t transform_direction; /* BFFT_FORWARD / BFFT_INVERSE                   */
+    int32_t norm;                /* BFFT_NORM_*                                   */
+    int32_t real_flow;           /* BFFT_REAL_COMPAT / BFFT_REAL_DEDICATED        */
+    int32_t block;               /* reference BLOCK; threads of stage kernels     */
+    int32_t tile;                /* local group / hybrid tile (0 = default)       */
+    int32_t rows;                /* M2 rows (tile-blocks per program)             */
+    int32_t glog, maxp, cells;   /* M3 grouping knobs (matrices.py:373-405)       */
+    int32_t variant;             /* BFFT_SPREAD / BFFT_FOLDED                     */
+    int32_t device;              /* CUDA device ordinal                           */
+} bfft_plan_desc;
+
+typedef struct bfft_plan_s* bfft_plan_t;
+
+/* API version (BFFT_API_VERSION of the built library). */
+BFFT_EXPORT int bfft_api_version(void);
+
+/* Thread-local message of the last failed call on this thread ("" if none). */
+BFFT_EXPORT const char* bfft_last_error(void);
+
+/* Create a plan: validates the descriptor (before any launch), allocates the
+ * plan-owned twiddle tables on desc->device and returns the handle.
+ * Replaces plan_fft's execution-side state (entry.py:292-426, the per-plan
+ * caches of runner.py:298 / :507 and adapter_hybrid.py:62-86). */
+BFFT_EXPORT bfft_status bfft_plan_create(const bfft_plan_desc* desc, bfft_plan_t* plan);
+
+/* Bytes of caller-provided device workspace bfft_execute needs (may be 0). */
+BFFT_EXPORT bfft_status bfft_plan_workspace_size(bfft_plan_t plan, size_t* bytes);
+
+/* Number of kernel launches one bfft_execute of this plan enqueues. */
+BFFT_EXPORT bfft_status bfft_plan_launches(bfft_plan_t plan, int* launches);
+
+/* Execute the plan: in (B, N_in) -> out (B, N_out) with N_in / N_out the
+ * transform-type shapes of entry.py:459-498.  Replaces execute_fft_plan
+ * (entry.py:501-628): inverse conjugation, the norm epilogue and the real
+ * pack / stitch / pre-twiddle / unpack all run inside this call. */
+BFFT_EXPORT bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* Release a plan and its twiddle tables. */
+BFFT_EXPORT bfft_status bfft_plan_destroy(bfft_plan_t plan);
+
+/* Y[b, i] = X[b, bitrev(i)] over (batch, n) complex64
+ * (runner.py:1542-1552 bit_reverse_permute, kernels.py:81-97). */
+BFFT_EXPORT bfft_status bfft_bit_reverse_permute(const void* x, void* y, int64_t n, int64_t batch,
+                                     int32_t device, void* stream);
+
+/* Dedicated real-transform epilogues as stand-alone calls
+ * (runner.py:1687-1767, kernels.py:1127-1258).  z / u: (batch, n/2)
+ * complex64; x: (batch, n/2+1) complex64; out: (batch, n) float32. */
+BFFT_EXPORT bfft_status bfft_r2c_stitch(const void* z, void* x, int64_t n, int64_t batch, float scale,
+                            int32_t device, void* stream);
+BFFT_EXPORT bfft_status bfft_c2r_pre(const void* xh, void* z, int64_t n, int64_t batch, int32_t device,
+                         void* stream);
+BFFT_EXPORT bfft_status bfft_c2r_unpack(const void* u, void* out, int64_t n, int64_t batch, float scale,
+                            int32_t device, void* stream);
+
+/* Twiddle table of the reference (runner.py:93-97 twiddle_tables):
+ * w[idx] = exp(-2 pi i idx / n) for idx < count, complex64, computed in
+ * float64 and rounded once. */
+BFFT_EXPORT bfft_status bfft_twiddle_table(void* w, int64_t n, int64_t count, int32_t device, void* stream);
+
+/* Device index maps used by the kernels, written for i < 2^bits into the
+ * uint32 device array `out`: kind 0 bit reversal (kernels.py:27-38),
+ * 1 DIT radix-4 digit reversal (:41-57), 2 DIF digit reversal (:60-78). */
+BFFT_EXPORT bfft_status bfft_index_map(int32_t kind, int32_t bits, void* out, int32_t device, void* stream);
+
+/* Total kernels this library has enqueued in this process (all devices). */
+BFFT_EXPORT uint64_t bfft_launch_counter(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BFFT_H */

@@ -1,0 +1,155 @@
+"""ctypes binding of libbfft.so (the C ABI declared in include/bfft.h).
+
+The Python layer reaches the GPU only through these entry points.  There is
+no fallback: if the library is missing or cannot be loaded, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+import weakref
+
+from . import _build
+
+OK, ERR_VALUE, ERR_SHAPE, ERR_UNSUPPORTED, ERR_CUDA, ERR_NCCL, ERR_ALLOC, ERR_WORKSPACE = range(8)
+
+RUNNER_IDS = {
+    "fft_dit": 0, "fft_dif": 1, "fft_dit_batch": 2, "fft_dif_batch": 3,
+    "fft_dit_radix4": 4, "fft_dif_radix4": 5, "fft_dit_radix4_batch": 6, "fft_dif_radix4_batch": 7,
+    "fft_dit_fused": 8, "fft_dit_matrix": 9, "fft_dif_matrix": 10, "fft_dit_matrix_batch": 11,
+    "fft_dif_matrix_batch": 12, "fft_dit_grouped": 13, "fft_dif_grouped": 14, "run_hybrid": 15,
+}
+TRANSFORM_TYPE_IDS = {"c2c": 0, "r2c": 1, "c2r": 2}
+TRANSFORM_DIRECTION_IDS = {"forward": 0, "inverse": 1}
+NORM_IDS = {"none": 0, "forward": 1, "backward": 2, "ortho": 3}
+VARIANT_IDS = {"spread": 0, "folded": 1}
+
+# Every symbol include/bfft.h declares.
+EXPORTS = ("bfft_api_version", "bfft_last_error", "bfft_plan_create", "bfft_plan_workspace_size",
+           "bfft_plan_launches", "bfft_execute", "bfft_plan_destroy", "bfft_bit_reverse_permute",
+           "bfft_r2c_stitch", "bfft_c2r_pre", "bfft_c2r_unpack", "bfft_twiddle_table",
+           "bfft_index_map", "bfft_launch_counter")
+
+
+class PlanDesc(ctypes.Structure):
+    """Mirror of struct bfft_plan_desc."""
+
+    _fields_ = [("runner", ctypes.c_int32), ("direction", ctypes.c_int32),
+                ("n", ctypes.c_int64), ("batch", ctypes.c_int64),
+                ("transform_type", ctypes.c_int32), ("transform_direction", ctypes.c_int32),
+                ("norm", ctypes.c_int32), ("real_flow", ctypes.c_int32),
+                ("block", ctypes.c_int32), ("tile", ctypes.c_int32), ("rows", ctypes.c_int32),
+                ("glog", ctypes.c_int32), ("maxp", ctypes.c_int32), ("cells", ctypes.c_int32),
+                ("variant", ctypes.c_int32), ("device", ctypes.c_int32)]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def library_path() -> str:
+    return _build.LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load libbfft.so (raises RuntimeError when it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = library_path()
+        if not os.path.exists(path):
+            raise RuntimeError(f"libbfft.so not found at {path}; build it with "
+                               "bfft._build.build() (nvcc, sm_100a) -- there is no CPU fallback")
+        L = ctypes.CDLL(path)
+        vp, i64, i32, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_size_t
+        L.bfft_api_version.restype = ctypes.c_int
+        L.bfft_last_error.restype = ctypes.c_char_p
+        L.bfft_launch_counter.restype = ctypes.c_uint64
+        L.bfft_plan_create.argtypes = [ctypes.POINTER(PlanDesc), ctypes.POINTER(vp)]
+        L.bfft_plan_workspace_size.argtypes = [vp, ctypes.POINTER(sz)]
+        L.bfft_plan_launches.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
+        L.bfft_execute.argtypes = [vp, vp, vp, vp, sz, vp]
+        L.bfft_plan_destroy.argtypes = [vp]
+        L.bfft_bit_reverse_permute.argtypes = [vp, vp, i64, i64, i32, vp]
+        L.bfft_r2c_stitch.argtypes = [vp, vp, i64, i64, ctypes.c_float, i32, vp]
+        L.bfft_c2r_pre.argtypes = [vp, vp, i64, i64, i32, vp]
+        L.bfft_c2r_unpack.argtypes = [vp, vp, i64, i64, ctypes.c_float, i32, vp]
+        L.bfft_twiddle_table.argtypes = [vp, i64, i64, i32, vp]
+        L.bfft_index_map.argtypes = [i32, i32, vp, i32, vp]
+        for name in EXPORTS:
+            fn = getattr(L, name)
+            if name not in ("bfft_api_version", "bfft_last_error", "bfft_launch_counter"):
+                fn.restype = ctypes.c_int
+        _lib = L
+        return L
+
+
+def last_error() -> str:
+    msg = load().bfft_last_error()
+    return msg.decode(errors="replace") if msg else ""
+
+
+def check(status: int, what: str = "bfft") -> None:
+    """Map a bfft_status onto the reference's exception types."""
+    if status == OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if status in (ERR_VALUE, ERR_SHAPE, ERR_UNSUPPORTED, ERR_WORKSPACE):
+        raise ValueError(msg)
+    if status == ERR_ALLOC:
+        raise MemoryError(msg)
+    raise RuntimeError(msg)
+
+
+def launch_counter() -> int:
+    return int(load().bfft_launch_counter())
+
+
+def _destroy(handle: int) -> None:
+    try:
+        if _lib is not None and handle:
+            _lib.bfft_plan_destroy(ctypes.c_void_p(handle))
+    except Exception:  # noqa: BLE001 - interpreter shutdown
+        pass
+
+
+class NativePlan:
+    """Owns one bfft_plan_t; destroyed with the Python object."""
+
+    def __init__(self, desc: PlanDesc):
+        L = load()
+        h = ctypes.c_void_p()
+        check(L.bfft_plan_create(ctypes.byref(desc), ctypes.byref(h)), "bfft_plan_create")
+        self.handle = h.value
+        self.desc = desc
+        ws = ctypes.c_size_t()
+        check(L.bfft_plan_workspace_size(self.handle, ctypes.byref(ws)), "bfft_plan_workspace_size")
+        self.workspace_bytes = int(ws.value)
+        nl = ctypes.c_int()
+        check(L.bfft_plan_launches(self.handle, ctypes.byref(nl)), "bfft_plan_launches")
+        self.launches = int(nl.value)
+        self._fin = weakref.finalize(self, _destroy, self.handle)
+
+    def execute(self, in_ptr: int, out_ptr: int, ws_ptr: int, ws_bytes: int, stream: int) -> None:
+        check(load().bfft_execute(self.handle, in_ptr, out_ptr, ws_ptr, ws_bytes, stream),
+              "bfft_execute")
+
+
+def make_desc(runner: str, direction: str, n: int, batch: int, *, transform_type: str = "c2c",
+              transform_direction: str = "forward", norm: str = "backward", real_flow: bool = False,
+              block: int = 256, tile: int = 0, rows: int = 0, glog: int = 2, maxp: int = 4096,
+              cells: int = 1, variant: str = "spread", device: int = 0) -> PlanDesc:
+    if runner not in RUNNER_IDS:
+        raise ValueError(f"unknown runner {runner!r}")
+    if variant not in VARIANT_IDS:
+        raise ValueError(f"variant must be 'spread' or 'folded', got {variant!r}")
+    return PlanDesc(runner=RUNNER_IDS[runner], direction=0 if direction == "dit" else 1, n=int(n),
+                    batch=int(batch), transform_type=TRANSFORM_TYPE_IDS[transform_type],
+                    transform_direction=TRANSFORM_DIRECTION_IDS[transform_direction],
+                    norm=NORM_IDS[norm], real_flow=1 if real_flow else 0, block=int(block),
+                    tile=int(tile), rows=int(rows), glog=int(glog), maxp=int(maxp),
+                    cells=int(cells), variant=VARIANT_IDS[variant], device=int(device))

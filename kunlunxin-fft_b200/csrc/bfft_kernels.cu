@@ -1,0 +1,637 @@
+// bfft_kernels.cu -- sm_100a kernels of the B200 FFT library.
+//
+// Two kernel families:
+//   * global-stage kernels: one radix-2 or radix-4 stage per launch over the
+//     whole (B, N) array -- the B200 realisation of the reference's M0/M4/M5
+//     flows, with the same index maps, twiddle exponents and folded
+//     permutations (src/xpu/kernels.py:100-423, :633-1124);
+//   * the CTA-resident Stockham pass: a whole sub-FFT of up to 4096 points is
+//     loaded once from HBM into registers, transformed with radix-16 register
+//     butterflies whose stages exchange through padded shared memory, and
+//     stored once.  One pass is a complete FFT for N <= 4096; larger N and the
+//     reference's local-group / grouped-tail / 4-step flows are sequences of
+//     such passes with fused twiddles.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "bfft_kernels.cuh"
+
+namespace bfft {
+
+// ============================================================== twiddle tables
+
+__device__ float2 g_tw_levels[2 * kTwUnit];
+
+__global__ void k_twiddle_levels() {
+    int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx < 1 || idx >= 2 * kTwUnit) return;
+    int lp = 1 << (31 - __clz(idx));  // level: idx in [lp, 2 lp)
+    int e = idx - lp;
+    double s, c;
+    sincospi(2.0 * (double)e / (double)lp, &s, &c);
+    g_tw_levels[idx] = make_float2((float)c, (float)(-s));
+}
+
+__global__ void k_twiddle_two_level(float2* lo, float2* hi, int lo_bits, int log2n) {
+    int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t nlo = (int64_t)1 << (lo_bits < log2n ? lo_bits : log2n);
+    int64_t nhi = log2n > lo_bits ? ((int64_t)1 << (log2n - lo_bits)) : 0;
+    double inv_n = 1.0 / (double)((int64_t)1 << log2n);  // exact: power of two
+    double s, c;
+    if (idx < nlo) {
+        sincospi(2.0 * (double)idx * inv_n, &s, &c);
+        lo[idx] = make_float2((float)c, (float)(-s));
+    } else if (idx < nlo + nhi) {
+        int64_t h = idx - nlo;
+        sincospi(2.0 * (double)(h << lo_bits) * inv_n, &s, &c);
+        hi[h] = make_float2((float)c, (float)(-s));
+    }
+}
+
+static std::mutex g_tw_mu;
+static bool g_tw_ready[64];
+
+cudaError_t ensure_unit_twiddles(int device, cudaStream_t stream) {
+    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(g_tw_mu);
+    if (g_tw_ready[device]) return cudaSuccess;
+    k_twiddle_levels<<<(2 * kTwUnit + 255) / 256, 256, 0, stream>>>();
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e == cudaSuccess) g_tw_ready[device] = true;
+    return e;
+}
+
+cudaError_t fill_two_level(float2* lo, float2* hi, int lo_bits, int log2n, cudaStream_t s) {
+    int64_t nlo = (int64_t)1 << (lo_bits < log2n ? lo_bits : log2n);
+    int64_t nhi = log2n > lo_bits ? ((int64_t)1 << (log2n - lo_bits)) : 0;
+    int64_t tot = nlo + nhi;
+    k_twiddle_two_level<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(lo, hi, lo_bits, log2n);
+    return cudaGetLastError();
+}
+
+// ============================================================== global stages
+
+__device__ __forceinline__ float2 ld_c(const float2* p, int conj) {
+    float2 v = __ldg(p);
+    return conj ? cconj(v) : v;
+}
+__device__ __forceinline__ float2 out_c(float2 v, int conj, float scale) {
+    if (conj) v = cconj(v);
+    return scale != 1.0f ? cscale(v, scale) : v;
+}
+__device__ __forceinline__ int64_t perm_out(int64_t i, int mode, int bits) {
+    return mode == 1 ? (int64_t)brev_bits((uint32_t)i, bits)
+         : mode == 2 ? (int64_t)dif_digit_reverse((uint32_t)i, bits) : i;
+}
+
+// One radix-2 stage (src/xpu/kernels.py:100-236, :993-1124):
+//   off in [0, N/2): j = off % n, i = (off / n) * 2n + j, w = W_N^{j*M}
+//   DIT: y[i] = a + b w, y[i+n] = a - b w   (a, b optionally bit-reversed reads)
+//   DIF: y[P(i)] = a + b, y[P(i+n)] = (a - b) w
+template <bool DIF>
+__device__ __forceinline__ void radix2_body(const float2* __restrict__ x, float2* __restrict__ y,
+                                            const StageArgs& a, int64_t row, int64_t off,
+                                            int log2half) {
+    const float2* xr = x + row * a.n;
+    float2* yr = y + row * a.n;
+    const int64_t n = a.half;
+    const int64_t j = off & (n - 1);
+    const int64_t i = ((off >> log2half) << (log2half + 1)) + j;
+    const float2 w = tw_two_level(a.tw, (uint64_t)(j * a.M));
+    int64_t s0 = i, s1 = i + n;
+    if (!DIF && a.in_perm == 1) {
+        s0 = brev_bits((uint32_t)s0, a.log2n);
+        s1 = brev_bits((uint32_t)s1, a.log2n);
+    }
+    float2 va = ld_c(xr + s0, a.conj_in), vb = ld_c(xr + s1, a.conj_in);
+    if (!DIF) {
+        float2 bw = cmul(vb, w);
+        yr[i] = out_c(cadd(va, bw), a.conj_out, a.scale);
+        yr[i + n] = out_c(csub(va, bw), a.conj_out, a.scale);
+    } else {
+        float2 sm = cadd(va, vb);
+        float2 df = cmul(csub(va, vb), w);
+        yr[perm_out(i, a.out_perm, a.log2n)] = out_c(sm, a.conj_out, a.scale);
+        yr[perm_out(i + n, a.out_perm, a.log2n)] = out_c(df, a.conj_out, a.scale);
+    }
+}
+
+template <bool DIF>
+__global__ void k_radix2_stage(const float2* __restrict__ x, float2* __restrict__ y, StageArgs a) {
+    const int64_t half_n = a.n >> 1;
+    const int log2half = 63 - __clzll(a.half);
+    if (a.folded) {
+        const int64_t total = a.batch * half_n;
+        for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+             g += (int64_t)gridDim.x * blockDim.x)
+            radix2_body<DIF>(x, y, a, g >> (a.log2n - 1), g & (half_n - 1), log2half);
+    } else {
+        const int64_t off = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+        if (off >= half_n) return;
+        for (int64_t row = blockIdx.y; row < a.batch; row += gridDim.y)
+            radix2_body<DIF>(x, y, a, row, off, log2half);
+    }
+}
+
+// One radix-4 stage of span 4n (src/xpu/kernels.py:239-423, :633-809):
+//   off in [0, N/4): j = off % n, i = (off / n) * 4n + j, exponents d*j*M.
+//   DIT: twiddle inputs then 4-point DFT (optional digit-reversed reads).
+//   DIF: 4-point DFT then twiddle outputs (optional digit-reversed stores).
+template <bool DIF>
+__device__ __forceinline__ void radix4_body(const float2* __restrict__ x, float2* __restrict__ y,
+                                            const StageArgs& a, int64_t row, int64_t off,
+                                            int log2q) {
+    const float2* xr = x + row * a.n;
+    float2* yr = y + row * a.n;
+    const int64_t n = a.half;
+    const int64_t j = off & (n - 1);
+    const int64_t i = ((off >> log2q) << (log2q + 2)) + j;
+    const uint64_t jm = (uint64_t)(j * a.M);
+    float2 v[4];
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+        int64_t s = i + d * n;
+        if (!DIF && a.in_perm == 2) s = dit_digit_reverse((uint32_t)s, a.log2n);
+        v[d] = ld_c(xr + s, a.conj_in);
+    }
+    if (!DIF) {
+#pragma unroll
+        for (int d = 1; d < 4; ++d) v[d] = cmul(v[d], tw_two_level(a.tw, jm * d));
+    }
+    // 4-point DFT in the reference's column order (y0..y3)
+    float2 y0 = cadd(cadd(v[0], v[1]), cadd(v[2], v[3]));
+    float2 y1 = make_float2(v[0].x + v[1].y - v[2].x - v[3].y, v[0].y - v[1].x - v[2].y + v[3].x);
+    float2 y2 = make_float2(v[0].x - v[1].x + v[2].x - v[3].x, v[0].y - v[1].y + v[2].y - v[3].y);
+    float2 y3 = make_float2(v[0].x - v[1].y - v[2].x + v[3].y, v[0].y + v[1].x - v[2].y - v[3].x);
+    float2 o[4] = {y0, y1, y2, y3};
+    if (DIF) {
+#pragma unroll
+        for (int d = 1; d < 4; ++d) o[d] = cmul(o[d], tw_two_level(a.tw, jm * d));
+    }
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+        int64_t dst = i + d * n;
+        if (DIF && a.out_perm == 2) dst = dif_digit_reverse((uint32_t)dst, a.log2n);
+        yr[dst] = out_c(o[d], a.conj_out, a.scale);
+    }
+}
+
+template <bool DIF>
+__global__ void k_radix4_stage(const float2* __restrict__ x, float2* __restrict__ y, StageArgs a) {
+    const int64_t quarter = a.n >> 2;
+    const int log2q = 63 - __clzll(a.half);
+    if (a.folded) {
+        const int64_t total = a.batch * quarter;
+        for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+             g += (int64_t)gridDim.x * blockDim.x)
+            radix4_body<DIF>(x, y, a, g >> (a.log2n - 2), g & (quarter - 1), log2q);
+    } else {
+        const int64_t off = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+        if (off >= quarter) return;
+        for (int64_t row = blockIdx.y; row < a.batch; row += gridDim.y)
+            radix4_body<DIF>(x, y, a, row, off, log2q);
+    }
+}
+
+static int clamp_block(int block) {
+    if (block < 32) return 32;
+    if (block > 1024) return 1024;
+    return block;
+}
+
+static dim3 stage_grid(int64_t per_row, int64_t batch, int block, bool folded) {
+    if (folded) {
+        int64_t blocks = (per_row * batch + block - 1) / block;
+        if (blocks > 148 * 64) blocks = 148 * 64;
+        return dim3((unsigned)(blocks < 1 ? 1 : blocks));
+    }
+    int64_t bx = (per_row + block - 1) / block;
+    int64_t by = batch < 65535 ? batch : 65535;
+    return dim3((unsigned)bx, (unsigned)by);
+}
+
+cudaError_t launch_radix2_stage(bool dif, const float2* x, float2* y, const StageArgs& a,
+                                int block, cudaStream_t s) {
+    block = clamp_block(block);
+    dim3 g = stage_grid(a.n >> 1, a.batch, block, a.folded != 0);
+    if (dif)
+        k_radix2_stage<true><<<g, block, 0, s>>>(x, y, a);
+    else
+        k_radix2_stage<false><<<g, block, 0, s>>>(x, y, a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_radix4_stage(bool dif, const float2* x, float2* y, const StageArgs& a,
+                                int block, cudaStream_t s) {
+    block = clamp_block(block);
+    dim3 g = stage_grid(a.n >> 2, a.batch, block, a.folded != 0);
+    if (dif)
+        k_radix4_stage<true><<<g, block, 0, s>>>(x, y, a);
+    else
+        k_radix4_stage<false><<<g, block, 0, s>>>(x, y, a);
+    return cudaGetLastError();
+}
+
+// ============================================================== permutation / epilogues
+
+// Y[r, i] = X[r, bitrev(i)]  (src/xpu/kernels.py:81-97, :536-561), with an
+// optional conjugate and scale folded into the store.
+__global__ void k_bitrev(const float2* __restrict__ x, float2* __restrict__ y, int64_t n,
+                         int64_t total, int log2n, int conj, float scale) {
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+         g += (int64_t)gridDim.x * blockDim.x) {
+        int64_t row = g >> log2n, i = g & (n - 1);
+        y[g] = out_c(__ldg(x + row * n + brev_bits((uint32_t)i, log2n)), conj, scale);
+    }
+}
+
+static unsigned flat_grid(int64_t total, int block) {
+    int64_t b = (total + block - 1) / block;
+    if (b > 148 * 32) b = 148 * 32;
+    return (unsigned)(b < 1 ? 1 : b);
+}
+
+cudaError_t launch_bitrev(const float2* x, float2* y, int64_t n, int64_t batch, int block,
+                          cudaStream_t s, int conj, float scale) {
+    block = clamp_block(block);
+    int log2n = 63 - __builtin_clzll((unsigned long long)n);
+    k_bitrev<<<flat_grid(n * batch, block), block, 0, s>>>(x, y, n, n * batch, log2n, conj, scale);
+    return cudaGetLastError();
+}
+
+// Packed-compat helpers of the real transforms (src/xpu/entry.py:588-616):
+// real -> complex with zero imaginary part, half-spectrum crop with scale,
+// Hermitian rebuild (entry.py:671-696) with the inverse conjugation folded
+// in, and the real-part extraction of the conjugated, scaled result.
+__global__ void k_real_to_complex(const float* __restrict__ x, float2* __restrict__ y, int64_t total) {
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+         g += (int64_t)gridDim.x * blockDim.x)
+        y[g] = make_float2(__ldg(x + g), 0.0f);
+}
+
+__global__ void k_crop(const float2* __restrict__ y, float2* __restrict__ out, int64_t n,
+                       int64_t cols, int64_t total, float scale) {
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+         g += (int64_t)gridDim.x * blockDim.x) {
+        int64_t b = g / cols, k = g - b * cols;
+        out[g] = cscale(__ldg(y + b * n + k), scale);
+    }
+}
+
+__global__ void k_hermitian_conj(const float2* __restrict__ xh, float2* __restrict__ full,
+                                 int64_t n, int64_t total) {
+    const int64_t m = n / 2 + 1;
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+         g += (int64_t)gridDim.x * blockDim.x) {
+        int64_t b = g / n, k = g - b * n;
+        float2 v;
+        if (k < m) {
+            v = __ldg(xh + b * m + k);
+            if (k == 0 || k == m - 1) v.y = 0.0f;
+        } else {
+            v = cconj(__ldg(xh + b * m + (n - k)));
+        }
+        full[g] = cconj(v);  // inverse via the conjugate trick
+    }
+}
+
+__global__ void k_real_part(const float2* __restrict__ y, float* __restrict__ out, int64_t total,
+                            float scale) {
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+         g += (int64_t)gridDim.x * blockDim.x)
+        out[g] = __ldg(y + g).x * scale;
+}
+
+cudaError_t launch_real_to_complex(const float* x, float2* y, int64_t total, cudaStream_t s) {
+    k_real_to_complex<<<flat_grid(total, 256), 256, 0, s>>>(x, y, total);
+    return cudaGetLastError();
+}
+cudaError_t launch_crop(const float2* y, float2* out, int64_t n, int64_t batch, float scale,
+                        cudaStream_t s) {
+    int64_t cols = n / 2 + 1;
+    k_crop<<<flat_grid(batch * cols, 256), 256, 0, s>>>(y, out, n, cols, batch * cols, scale);
+    return cudaGetLastError();
+}
+cudaError_t launch_hermitian_conj(const float2* xh, float2* full, int64_t n, int64_t batch,
+                                  cudaStream_t s) {
+    k_hermitian_conj<<<flat_grid(batch * n, 256), 256, 0, s>>>(xh, full, n, batch * n);
+    return cudaGetLastError();
+}
+cudaError_t launch_real_part(const float2* y, float* out, int64_t total, float scale,
+                             cudaStream_t s) {
+    k_real_part<<<flat_grid(total, 256), 256, 0, s>>>(y, out, total, scale);
+    return cudaGetLastError();
+}
+
+// The kernels' index maps, materialised for bit-exact checks.
+__global__ void k_index_map(int kind, int bits, uint32_t* out) {
+    const uint32_t n = 1u << bits;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        out[i] = kind == 0 ? brev_bits(i, bits) : kind == 1 ? dit_digit_reverse(i, bits)
+                                                            : dif_digit_reverse(i, bits);
+}
+cudaError_t launch_index_map(int kind, int bits, uint32_t* out, cudaStream_t s) {
+    k_index_map<<<flat_grid((int64_t)1 << bits, 256), 256, 0, s>>>(kind, bits, out);
+    return cudaGetLastError();
+}
+
+// Reference twiddle table as complex64: w[idx] = W_n^idx, idx < count
+// (src/xpu/runner.py:93-97), float64 angles rounded once.
+__global__ void k_twiddle_table(float2* w, int64_t n, int64_t count) {
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < count;
+         g += (int64_t)gridDim.x * blockDim.x) {
+        double s, c;
+        sincospi(2.0 * (double)g / (double)n, &s, &c);
+        w[g] = make_float2((float)c, (float)(-s));
+    }
+}
+cudaError_t launch_twiddle_table(float2* w, int64_t n, int64_t count, cudaStream_t s) {
+    k_twiddle_table<<<flat_grid(count, 256), 256, 0, s>>>(w, n, count);
+    return cudaGetLastError();
+}
+
+// R2C stitch (src/xpu/kernels.py:1127-1177): from the N/2-point FFT Z of the
+// packed pairs, X[k] = a - i w c, a = (Z[k] + conj Z[j]) / 2,
+// c = (Z[k] - conj Z[j]) / 2, j = (N/2 - k) % (N/2), w = W_N^k; DC and
+// Nyquist imaginary parts are exactly 0; scale fused into the store.
+__device__ __forceinline__ float2 r2c_point(const float2* zb, int64_t np, int64_t k, float2 w,
+                                            float scale) {
+    const int64_t jc = (np - k) & (np - 1), zk = k & (np - 1);
+    const float2 zkv = zb[zk], zjv = zb[jc];
+    const float ar = 0.5f * (zkv.x + zjv.x), ai = 0.5f * (zkv.y - zjv.y);
+    const float cr = 0.5f * (zkv.x - zjv.x), ci = 0.5f * (zkv.y + zjv.y);
+    float xr = ar + w.x * ci + w.y * cr;
+    float xi = ai - w.x * cr + w.y * ci;
+    if (k == 0 || k == np) xi = 0.0f;
+    return make_float2(xr * scale, xi * scale);
+}
+
+__global__ void k_r2c_stitch(const float2* __restrict__ z, float2* __restrict__ x, int64_t n,
+                             int64_t batch, float scale, TwoLevel twn) {
+    const int64_t np = n >> 1, cols = np + 1, total = batch * cols;
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+         g += (int64_t)gridDim.x * blockDim.x) {
+        int64_t b = g / cols, k = g - b * cols;
+        x[g] = r2c_point(z + b * np, np, k, tw_two_level(twn, (uint64_t)k), scale);
+    }
+}
+
+// C2R pre-twiddle (src/xpu/kernels.py:1180-1229): Z[k] = a + i w c with
+// w = conj(W_N^k), DC / Nyquist imaginary parts ignored.
+__device__ __forceinline__ float2 c2r_pre_point(const float2* xb, int64_t np, int64_t k, float2 w) {
+    const int64_t j = np - k;
+    float2 xk = xb[k], xj = xb[j];
+    if (k == 0) xk.y = 0.0f;
+    if (j == np) xj.y = 0.0f;
+    const float ar = 0.5f * (xk.x + xj.x), ai = 0.5f * (xk.y - xj.y);
+    const float cr = 0.5f * (xk.x - xj.x), ci = 0.5f * (xk.y + xj.y);
+    const float wr = w.x, wi = -w.y;
+    return make_float2(ar - (wr * ci + wi * cr), ai + (wr * cr - wi * ci));
+}
+
+__global__ void k_c2r_pre(const float2* __restrict__ xh, float2* __restrict__ z, int64_t n,
+                          int64_t batch, TwoLevel twn) {
+    const int64_t np = n >> 1, cols = np + 1, total = batch * np;
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+         g += (int64_t)gridDim.x * blockDim.x) {
+        int64_t b = g / np, k = g - b * np;
+        z[g] = c2r_pre_point(xh + b * cols, np, k, tw_two_level(twn, (uint64_t)k));
+    }
+}
+
+// C2R unpack (src/xpu/kernels.py:1232-1258): out[2k], out[2k+1] =
+// scale * (Re, Im) u[(N/2 - k) % (N/2)].
+__global__ void k_c2r_unpack(const float2* __restrict__ u, float2* __restrict__ out, int64_t n,
+                             int64_t batch, float scale) {
+    const int64_t np = n >> 1, total = batch * np;
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+         g += (int64_t)gridDim.x * blockDim.x) {
+        int64_t b = g / np, k = g - b * np;
+        float2 v = u[b * np + ((np - k) & (np - 1))];
+        out[g] = make_float2(v.x * scale, v.y * scale);
+    }
+}
+
+__global__ void k_scale(const float2* __restrict__ x, float2* __restrict__ y, int64_t count,
+                        float scale, int conj) {
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < count;
+         g += (int64_t)gridDim.x * blockDim.x)
+        y[g] = out_c(x[g], conj, scale);
+}
+
+cudaError_t launch_r2c_stitch(const float2* z, float2* x, int64_t n, int64_t batch, float scale,
+                              TwoLevel twn, cudaStream_t s) {
+    k_r2c_stitch<<<flat_grid(batch * (n / 2 + 1), 256), 256, 0, s>>>(z, x, n, batch, scale, twn);
+    return cudaGetLastError();
+}
+cudaError_t launch_c2r_pre(const float2* xh, float2* z, int64_t n, int64_t batch, TwoLevel twn,
+                           cudaStream_t s) {
+    k_c2r_pre<<<flat_grid(batch * (n / 2), 256), 256, 0, s>>>(xh, z, n, batch, twn);
+    return cudaGetLastError();
+}
+cudaError_t launch_c2r_unpack(const float2* u, float* out, int64_t n, int64_t batch, float scale,
+                              cudaStream_t s) {
+    k_c2r_unpack<<<flat_grid(batch * (n / 2), 256), 256, 0, s>>>(u, reinterpret_cast<float2*>(out),
+                                                                   n, batch, scale);
+    return cudaGetLastError();
+}
+cudaError_t launch_scale(const float2* x, float2* y, int64_t count, float scale, int conj,
+                         cudaStream_t s) {
+    k_scale<<<flat_grid(count, 256), 256, 0, s>>>(x, y, count, scale, conj);
+    return cudaGetLastError();
+}
+
+// ============================================================== Stockham pass
+
+template <int LOG2L, int LAYOUT, int STORE_T>
+struct PassGeo {
+    static constexpr int L = 1 << LOG2L;
+    static constexpr int E = L < 16 ? L : 16;          // elements per thread
+    static constexpr int TF = L / E;                   // threads per sub-FFT
+    static constexpr int KMIN = (LAYOUT || STORE_T) ? 4 : 1;
+    static constexpr int K0 = TF >= 256 ? 1 : 256 / TF;
+    static constexpr int K = K0 > KMIN ? K0 : KMIN;   // sub-FFTs per CTA
+    static constexpr int THREADS = K * TF;
+    static constexpr int LPAD = L + (L >> 4) + 1;      // odd region stride
+    static constexpr int NP = LOG2L <= 4 ? 1 : (LOG2L + 3) / 4;
+    static constexpr bool SMEM = NP > 1 || STORE_T;
+};
+
+__device__ __forceinline__ int pad16(int a) { return a + (a >> 4); }
+
+__host__ __device__ constexpr int radix_log2(int log2l, int pass) { return pass < log2l / 4 ? 4 : log2l % 4; }
+
+// Radix-R Stockham pass with p = 16^PASS (all earlier radices are 16):
+// butterfly b takes elements b + j L/R, twiddles them by W_{Rp}^{j (b mod p)},
+// runs an R-point DFT and sends output j to (b/p) p R + (b mod p) + j p.
+// Thread t owns elements t + m' TF (m' < E), so butterfly q of the thread
+// reads and writes slots q + j (E/R).
+template <int LOG2L, int PASS, int E, int TF>
+__device__ __forceinline__ void stockham_passes(float2 (&v)[E], int t, float2* region) {
+    constexpr int NP = LOG2L <= 4 ? 1 : (LOG2L + 3) / 4;
+    if constexpr (PASS < NP) {
+        constexpr int LR = radix_log2(LOG2L, PASS);
+        constexpr int R = 1 << LR;
+        constexpr int LP = 4 * PASS;
+        constexpr int NB = E / R;
+#pragma unroll
+        for (int q = 0; q < NB; ++q) {
+            const int b = t + q * TF;
+            const int k = b & ((1 << LP) - 1);
+            float2 u[R];
+#pragma unroll
+            for (int j = 0; j < R; ++j) u[j] = v[q + j * NB];
+            if constexpr (PASS > 0) {
+                const float2* tw = g_tw_levels + (R << LP);
+#pragma unroll
+                for (int j = 1; j < R; ++j) u[j] = cmul(u[j], __ldg(tw + j * k));
+            }
+            Dft<R>::run(u);
+#pragma unroll
+            for (int j = 0; j < R; ++j) v[q + j * NB] = u[j];
+        }
+        if constexpr (PASS + 1 < NP) {
+#pragma unroll
+            for (int q = 0; q < NB; ++q) {
+                const int b = t + q * TF;
+                const int k = b & ((1 << LP) - 1);
+                const int base = ((b >> LP) << (LP + LR)) + k;
+#pragma unroll
+                for (int j = 0; j < R; ++j) region[pad16(base + (j << LP))] = v[q + j * NB];
+            }
+            __syncthreads();
+#pragma unroll
+            for (int m = 0; m < E; ++m) v[m] = region[pad16(t + m * TF)];
+            __syncthreads();
+            stockham_passes<LOG2L, PASS + 1, E, TF>(v, t, region);
+        }
+    }
+}
+
+template <int LOG2L, int LAYOUT, int STORE_T>
+__global__ void __launch_bounds__(PassGeo<LOG2L, LAYOUT, STORE_T>::THREADS)
+    k_pass(const float2* __restrict__ in, float2* __restrict__ out, PassArgs a) {
+    using G = PassGeo<LOG2L, LAYOUT, STORE_T>;
+    extern __shared__ float2 smem[];
+    const int tid = threadIdx.x;
+    const int cl = LAYOUT ? tid % G::K : tid / G::TF;
+    const int t = LAYOUT ? tid / G::K : tid % G::TF;
+    const int64_t f = (int64_t)blockIdx.x * G::K + cl;
+    const bool active = f < a.nsub;
+    float2* region = smem + cl * G::LPAD;
+
+    int64_t o = 0, c = 0;
+    if (active) {
+        o = f / a.inner;
+        c = f - o * a.inner;
+    }
+    float2 v[G::E];
+    {
+        const int64_t cin = a.in_base_bits ? (int64_t)brev_bits((uint32_t)c, a.in_base_bits) : c;
+        const float2* src = in + o * a.in_outer + cin * a.in_inner;
+#pragma unroll
+        for (int m = 0; m < G::E; ++m) {
+            const int e = t + m * G::TF;
+            const int pe = a.in_elem_bitrev ? (int)brev_bits((uint32_t)e, LOG2L) : e;
+            float2 val = active ? __ldg(src + (int64_t)pe * a.in_stride) : make_float2(0.f, 0.f);
+            if (a.conj_in) val = cconj(val);
+            if (a.tw_mode == 1) val = cmul(val, tw_two_level(a.tw, (uint64_t)e * (uint64_t)c * (uint64_t)a.tw_mul));
+            v[m] = val;
+        }
+    }
+
+    stockham_passes<LOG2L, 0, G::E, G::TF>(v, t, region);
+
+#pragma unroll
+    for (int m = 0; m < G::E; ++m) {
+        const int k = t + m * G::TF;
+        float2 val = v[m];
+        if (a.tw_mode == 2) val = cmul(val, tw_two_level(a.tw, (uint64_t)k * (uint64_t)c * (uint64_t)a.tw_mul));
+        if (a.conj_out) val = cconj(val);
+        if (a.scale != 1.0f) val = cscale(val, a.scale);
+        v[m] = val;
+    }
+
+    if constexpr (!STORE_T) {
+        if (active) {
+            const int64_t cout = a.out_base_bits ? (int64_t)brev_bits((uint32_t)c, a.out_base_bits) : c;
+            float2* dst = out + o * a.out_outer + cout * a.out_inner;
+#pragma unroll
+            for (int m = 0; m < G::E; ++m) {
+                const int k = t + m * G::TF;
+                const int pk = a.out_elem_bitrev ? (int)brev_bits((uint32_t)k, LOG2L) : k;
+                dst[(int64_t)pk * a.out_stride] = v[m];
+            }
+        }
+    } else {
+        // Stage through shared memory, then store with the opposite thread
+        // layout: element index fastest after a column-layout compute (a
+        // contiguous output row per sub-FFT), sub-FFT index fastest after a
+        // row-layout compute (coalesced when out_inner == 1).
+#pragma unroll
+        for (int m = 0; m < G::E; ++m) region[pad16(t + m * G::TF)] = v[m];
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < G::E; ++i) {
+            const int idx = tid + i * G::THREADS;
+            const int cl2 = LAYOUT ? idx / G::L : idx % G::K;
+            const int k = LAYOUT ? idx % G::L : idx / G::K;
+            const int64_t f2 = (int64_t)blockIdx.x * G::K + cl2;
+            if (f2 < a.nsub) {
+                const int64_t o2 = f2 / a.inner, c2 = f2 - o2 * a.inner;
+                const int64_t cout = a.out_base_bits ? (int64_t)brev_bits((uint32_t)c2, a.out_base_bits) : c2;
+                const int pk = a.out_elem_bitrev ? (int)brev_bits((uint32_t)k, LOG2L) : k;
+                out[o2 * a.out_outer + cout * a.out_inner + (int64_t)pk * a.out_stride] =
+                    smem[cl2 * G::LPAD + pad16(k)];
+            }
+        }
+    }
+}
+
+template <int LOG2L, int LAYOUT, int STORE_T>
+static cudaError_t launch_pass_t(const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
+    using G = PassGeo<LOG2L, LAYOUT, STORE_T>;
+    const size_t smem = G::SMEM ? (size_t)G::K * G::LPAD * sizeof(float2) : 0;
+    auto kern = k_pass<LOG2L, LAYOUT, STORE_T>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    const int64_t ctas = (a.nsub + G::K - 1) / G::K;
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    kern<<<(unsigned)ctas, G::THREADS, smem, s>>>(in, out, a);
+    return cudaGetLastError();
+}
+
+template <int LOG2L>
+static cudaError_t launch_pass_l(int layout, int store_t, const float2* in, float2* out,
+                                 const PassArgs& a, cudaStream_t s) {
+    if (layout) {
+        return store_t ? launch_pass_t<LOG2L, 1, 1>(in, out, a, s) : launch_pass_t<LOG2L, 1, 0>(in, out, a, s);
+    }
+    return store_t ? launch_pass_t<LOG2L, 0, 1>(in, out, a, s) : launch_pass_t<LOG2L, 0, 0>(in, out, a, s);
+}
+
+cudaError_t launch_pass(int log2l, int layout, int store_t, const float2* in, float2* out,
+                        const PassArgs& a, cudaStream_t s) {
+    switch (log2l) {
+        case 1: return launch_pass_l<1>(layout, store_t, in, out, a, s);
+        case 2: return launch_pass_l<2>(layout, store_t, in, out, a, s);
+        case 3: return launch_pass_l<3>(layout, store_t, in, out, a, s);
+        case 4: return launch_pass_l<4>(layout, store_t, in, out, a, s);
+        case 5: return launch_pass_l<5>(layout, store_t, in, out, a, s);
+        case 6: return launch_pass_l<6>(layout, store_t, in, out, a, s);
+        case 7: return launch_pass_l<7>(layout, store_t, in, out, a, s);
+        case 8: return launch_pass_l<8>(layout, store_t, in, out, a, s);
+        case 9: return launch_pass_l<9>(layout, store_t, in, out, a, s);
+        case 10: return launch_pass_l<10>(layout, store_t, in, out, a, s);
+        case 11: return launch_pass_l<11>(layout, store_t, in, out, a, s);
+        case 12: return launch_pass_l<12>(layout, store_t, in, out, a, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace bfft
