@@ -338,6 +338,8 @@ def execute_fft_plan(plan: ExecutionPlan, x):
             raise ValueError(f"x must be on a CUDA device, got device={x.device}")
         if not x.is_contiguous():
             raise ValueError("x must be contiguous")
+        if x.data_ptr() % 8:
+            raise ValueError("x must start on an 8-byte boundary (complex64 / float32 pairs)")
         if plan.executed not in _lib.RUNNER_IDS:
             raise AssertionError(f"unmapped runner function {plan.executed!r}")
     dev = x.device.index if x.device.index is not None else torch.cuda.current_device()

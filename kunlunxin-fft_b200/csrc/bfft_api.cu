@@ -77,7 +77,7 @@ struct Step {
     bool dif = false;
     StageArgs st{};
     PassArgs pa{};
-    int log2l = 0, layout = 0, store_t = 0;
+    int log2l = 0, layout = 0, lmap = 0, smap = 0;
     int block = 256;
 };
 
@@ -143,14 +143,28 @@ Step stage4(bool dif, int64_t n, int64_t batch, int64_t span, int in_perm, int o
     return s;
 }
 
-Step pass_step(int log2l, int layout, int store_t, const PassArgs& pa) {
+// A pass step.  `transpose_store` asks for the store to be staged through
+// shared memory in the layout opposite to the compute layout.  Rows whose
+// tile is one contiguous block are copied cooperatively, and short
+// contiguous rows (fewer than 32 threads per sub-FFT) are stored staged too,
+// so every global access is coalesced across the warp.
+Step pass_step(int log2l, int layout, int transpose_store, const PassArgs& pa) {
     Step s;
     s.kind = S_PASS;
     s.log2l = log2l;
     s.layout = layout;
-    s.store_t = store_t;
     s.pa = pa;
     s.pa.scale = 1.0f;
+    s.pa.inner_log2 = ilog2(pa.inner);
+    const int64_t L = (int64_t)1 << log2l;
+    const int64_t tf = L < 16 ? 1 : L / 16;
+    s.smap = transpose_store ? (layout ? 1 : 2) : 0;
+    if (!layout) {
+        const bool contiguous_in = pa.in_stride == 1 && !pa.in_elem_bitrev && !pa.in_base_bits &&
+                                   pa.in_inner == L && pa.in_outer == pa.inner * L;
+        s.lmap = contiguous_in ? 1 : 0;
+        if (s.smap == 0 && tf < 32 && pa.out_stride == 1 && !pa.out_elem_bitrev) s.smap = 1;
+    }
     return s;
 }
 
@@ -478,7 +492,7 @@ cudaError_t launch_step(const Step& s, const float2* in, float2* out, cudaStream
     switch (s.kind) {
         case S_STAGE2: return launch_radix2_stage(s.dif, in, out, s.st, s.block, stream);
         case S_STAGE4: return launch_radix4_stage(s.dif, in, out, s.st, s.block, stream);
-        case S_PASS: return launch_pass(s.log2l, s.layout, s.store_t, in, out, s.pa, stream);
+        case S_PASS: return launch_pass(s.log2l, s.layout, s.lmap, s.smap, in, out, s.pa, stream);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -619,6 +633,8 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
     if (!plan) return fail(BFFT_ERR_VALUE, "null plan");
     if (!in || !out) return fail(BFFT_ERR_VALUE, "null input or output pointer");
     if (in == out) return fail(BFFT_ERR_VALUE, "input and output must not alias");
+    if (((uintptr_t)in | (uintptr_t)out | (uintptr_t)workspace) & 7u)
+        return fail(BFFT_ERR_VALUE, "input, output and workspace must be 8-byte aligned");
     if (plan->ws_bytes && (!workspace || workspace_bytes < plan->ws_bytes))
         return fail(BFFT_ERR_WORKSPACE, "workspace of %zu bytes required, got %zu", plan->ws_bytes,
                     workspace ? workspace_bytes : (size_t)0);
@@ -719,6 +735,7 @@ bfft_status bfft_bit_reverse_permute(const void* x, void* y, int64_t n, int64_t 
 static bfft_status real_epilogue_checks(const void* a, const void* b, int64_t n, int64_t batch) {
     if (!a || !b) return fail(BFFT_ERR_VALUE, "null pointer");
     if (a == b) return fail(BFFT_ERR_VALUE, "input and output must not alias");
+    if (((uintptr_t)a | (uintptr_t)b) & 7u) return fail(BFFT_ERR_VALUE, "pointers must be 8-byte aligned");
     if (!is_pow2(n)) return fail(BFFT_ERR_SHAPE, "size must be a positive power of two, got %lld", (long long)n);
     if (n < 4) return fail(BFFT_ERR_SHAPE, "dedicated real flow needs N >= 4, got %lld", (long long)n);
     if (batch < 1) return fail(BFFT_ERR_SHAPE, "batch must be >= 1");

@@ -159,9 +159,11 @@ struct TwoLevel {
     int log2n;
 };
 
-__device__ __forceinline__ float2 tw_two_level(const TwoLevel& t, uint64_t e) {
-    e &= (1ull << t.log2n) - 1ull;
-    float2 a = __ldg(t.lo + (e & ((1ull << t.lo_bits) - 1ull)));
+// Exponents are taken mod N (N | 2^32), so 32-bit wrap-around arithmetic on
+// the caller's side is exact.
+__device__ __forceinline__ float2 tw_two_level(const TwoLevel& t, uint32_t e) {
+    e &= (t.log2n >= 32) ? 0xffffffffu : ((1u << t.log2n) - 1u);
+    float2 a = __ldg(t.lo + (e & ((1u << t.lo_bits) - 1u)));
     if (t.log2n <= t.lo_bits) return a;
     float2 b = __ldg(t.hi + (e >> t.lo_bits));
     return cmul(a, b);

@@ -100,7 +100,7 @@ __device__ __forceinline__ void radix2_body(const float2* __restrict__ x, float2
     const int64_t n = a.half;
     const int64_t j = off & (n - 1);
     const int64_t i = ((off >> log2half) << (log2half + 1)) + j;
-    const float2 w = tw_two_level(a.tw, (uint64_t)(j * a.M));
+    const float2 w = tw_two_level(a.tw, (uint32_t)j * (uint32_t)a.M);
     int64_t s0 = i, s1 = i + n;
     if (!DIF && a.in_perm == 1) {
         s0 = brev_bits((uint32_t)s0, a.log2n);
@@ -149,7 +149,7 @@ __device__ __forceinline__ void radix4_body(const float2* __restrict__ x, float2
     const int64_t n = a.half;
     const int64_t j = off & (n - 1);
     const int64_t i = ((off >> log2q) << (log2q + 2)) + j;
-    const uint64_t jm = (uint64_t)(j * a.M);
+    const uint32_t jm = (uint32_t)j * (uint32_t)a.M;
     float2 v[4];
 #pragma unroll
     for (int d = 0; d < 4; ++d) {
@@ -159,7 +159,7 @@ __device__ __forceinline__ void radix4_body(const float2* __restrict__ x, float2
     }
     if (!DIF) {
 #pragma unroll
-        for (int d = 1; d < 4; ++d) v[d] = cmul(v[d], tw_two_level(a.tw, jm * d));
+        for (int d = 1; d < 4; ++d) v[d] = cmul(v[d], tw_two_level(a.tw, jm * (uint32_t)d));
     }
     // 4-point DFT in the reference's column order (y0..y3)
     float2 y0 = cadd(cadd(v[0], v[1]), cadd(v[2], v[3]));
@@ -169,7 +169,7 @@ __device__ __forceinline__ void radix4_body(const float2* __restrict__ x, float2
     float2 o[4] = {y0, y1, y2, y3};
     if (DIF) {
 #pragma unroll
-        for (int d = 1; d < 4; ++d) o[d] = cmul(o[d], tw_two_level(a.tw, jm * d));
+        for (int d = 1; d < 4; ++d) o[d] = cmul(o[d], tw_two_level(a.tw, jm * (uint32_t)d));
     }
 #pragma unroll
     for (int d = 0; d < 4; ++d) {
@@ -375,7 +375,7 @@ __global__ void k_r2c_stitch(const float2* __restrict__ z, float2* __restrict__ 
     for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
          g += (int64_t)gridDim.x * blockDim.x) {
         int64_t b = g / cols, k = g - b * cols;
-        x[g] = r2c_point(z + b * np, np, k, tw_two_level(twn, (uint64_t)k), scale);
+        x[g] = r2c_point(z + b * np, np, k, tw_two_level(twn, (uint32_t)k), scale);
     }
 }
 
@@ -398,7 +398,7 @@ __global__ void k_c2r_pre(const float2* __restrict__ xh, float2* __restrict__ z,
     for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
          g += (int64_t)gridDim.x * blockDim.x) {
         int64_t b = g / np, k = g - b * np;
-        z[g] = c2r_pre_point(xh + b * cols, np, k, tw_two_level(twn, (uint64_t)k));
+        z[g] = c2r_pre_point(xh + b * cols, np, k, tw_two_level(twn, (uint32_t)k));
     }
 }
 
@@ -445,20 +445,6 @@ cudaError_t launch_scale(const float2* x, float2* y, int64_t count, float scale,
 }
 
 // ============================================================== Stockham pass
-
-template <int LOG2L, int LAYOUT, int STORE_T>
-struct PassGeo {
-    static constexpr int L = 1 << LOG2L;
-    static constexpr int E = L < 16 ? L : 16;          // elements per thread
-    static constexpr int TF = L / E;                   // threads per sub-FFT
-    static constexpr int KMIN = (LAYOUT || STORE_T) ? 4 : 1;
-    static constexpr int K0 = TF >= 256 ? 1 : 256 / TF;
-    static constexpr int K = K0 > KMIN ? K0 : KMIN;   // sub-FFTs per CTA
-    static constexpr int THREADS = K * TF;
-    static constexpr int LPAD = L + (L >> 4) + 1;      // odd region stride
-    static constexpr int NP = LOG2L <= 4 ? 1 : (LOG2L + 3) / 4;
-    static constexpr bool SMEM = NP > 1 || STORE_T;
-};
 
 __device__ __forceinline__ int pad16(int a) { return a + (a >> 4); }
 
@@ -511,125 +497,230 @@ __device__ __forceinline__ void stockham_passes(float2 (&v)[E], int t, float2* r
     }
 }
 
-template <int LOG2L, int LAYOUT, int STORE_T>
-__global__ void __launch_bounds__(PassGeo<LOG2L, LAYOUT, STORE_T>::THREADS)
+__host__ __device__ constexpr int floor_pow2(int v) {
+    int p = 1;
+    while (p * 2 <= v) p *= 2;
+    return p;
+}
+
+// ---- asynchronous global -> shared copies (cp.async, 8 bytes) ----
+__device__ __forceinline__ void cp_async8(float2* sdst, const float2* gsrc) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(sdst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+
+// Persistent, software-pipelined pass.  Each CTA walks tiles of K sub-FFTs
+// (tile, tile + gridDim.x, ...).  Shared memory holds two padded tile
+// buffers: while tile i is transformed in buffer i&1 (its load stage, then its
+// exchange area, then its store stage), the copies of tile i+1 are already in
+// flight into the other buffer, so HBM reads overlap the arithmetic.
+//
+// LMAP 0: every thread copies exactly the elements it later owns (pattern
+//         t + m TF), so it only waits for its own copies;
+// LMAP 1: the tile is K*L contiguous elements and is copied cooperatively,
+//         element index fastest across the CTA (coalesced for tiny L).
+// SMAP 0: stores straight from registers;
+// SMAP 1: stores staged through shared memory, element index fastest;
+// SMAP 2: staged, sub-FFT index fastest (coalesced strided columns).
+template <int LOG2L, int LAYOUT, int LMAP, int SMAP>
+struct PassKGeo {
+    static constexpr int L = 1 << LOG2L;
+    static constexpr int E = L < 16 ? L : 16;
+    static constexpr int TF = L / E;
+    static constexpr int LPAD = L + (L >> 4) + 1;
+    // sub-FFTs per CTA: ~256 threads; >= 4 when the sub-FFT index is the
+    // coalesced dimension; capped so two tile buffers fit in 200 KB.
+    static constexpr int KMIN = (LAYOUT || SMAP == 2) ? 4 : 1;
+    static constexpr int K0 = TF >= 256 ? 1 : 256 / TF;
+    static constexpr int KD = K0 > KMIN ? K0 : KMIN;
+    static constexpr int KCAP = floor_pow2((200 * 1024) / (2 * LPAD * 8));
+    static constexpr int K = KD < KCAP ? KD : KCAP;
+    static constexpr int THREADS = K * TF;
+    // resident CTAs the register budget is sized for (~768 threads per SM)
+    static constexpr int MINB = THREADS >= 768 ? 1 : 768 / THREADS;
+    static constexpr int NP = LOG2L <= 4 ? 1 : (LOG2L + 3) / 4;
+    static constexpr size_t SMEM = (size_t)2 * K * LPAD * sizeof(float2) + (size_t)K * sizeof(int64_t);
+};
+
+template <int LOG2L, int LAYOUT, int LMAP, int SMAP>
+__global__ void __launch_bounds__(PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>::THREADS,
+                                  PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>::MINB)
     k_pass(const float2* __restrict__ in, float2* __restrict__ out, PassArgs a) {
-    using G = PassGeo<LOG2L, LAYOUT, STORE_T>;
-    extern __shared__ float2 smem[];
+    using G = PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>;
+    extern __shared__ __align__(16) float2 smem[];
+    int64_t* sbase = reinterpret_cast<int64_t*>(smem + 2 * G::K * G::LPAD);
     const int tid = threadIdx.x;
     const int cl = LAYOUT ? tid % G::K : tid / G::TF;
     const int t = LAYOUT ? tid / G::K : tid % G::TF;
-    const int64_t f = (int64_t)blockIdx.x * G::K + cl;
-    const bool active = f < a.nsub;
-    float2* region = smem + cl * G::LPAD;
+    const int64_t ntiles = (a.nsub + G::K - 1) / G::K;
+    const int64_t imask = (int64_t(1) << a.inner_log2) - 1;
+    const uint32_t in_stride = (uint32_t)a.in_stride, out_stride = (uint32_t)a.out_stride;
+    const float osr = a.scale, osi = a.conj_out ? -a.scale : a.scale;
 
-    int64_t o = 0, c = 0;
-    if (active) {
-        o = f / a.inner;
-        c = f - o * a.inner;
-    }
-    float2 v[G::E];
-    {
-        const int64_t cin = a.in_base_bits ? (int64_t)brev_bits((uint32_t)c, a.in_base_bits) : c;
-        const float2* src = in + o * a.in_outer + cin * a.in_inner;
+    auto issue = [&](int64_t tile, float2* buf) {
+        if (LMAP == 1) {
+            const float2* src = in + tile * (int64_t)(G::K * G::L);
+            const int64_t lim = (a.nsub - tile * G::K) * G::L;
+#pragma unroll
+            for (int i = 0; i < G::E; ++i) {
+                const int g = tid + i * G::THREADS;
+                if (g < lim) cp_async8(buf + (g >> LOG2L) * G::LPAD + pad16(g & (G::L - 1)), src + g);
+            }
+        } else {
+            const int64_t f = tile * G::K + cl;
+            if (f < a.nsub) {
+                const int64_t o = f >> a.inner_log2, c = f & imask;
+                const int64_t cin = a.in_base_bits ? (int64_t)brev_bits((uint32_t)c, a.in_base_bits) : c;
+                const float2* src = in + o * a.in_outer + cin * a.in_inner;
+                float2* dst = buf + cl * G::LPAD;
+#pragma unroll
+                for (int m = 0; m < G::E; ++m) {
+                    const uint32_t e = (uint32_t)(t + m * G::TF);
+                    const uint32_t pe = a.in_elem_bitrev ? brev_bits(e, LOG2L) : e;
+                    cp_async8(dst + pad16((int)e), src + pe * in_stride);
+                }
+            }
+        }
+    };
+
+    int64_t tile = blockIdx.x;
+    if (tile < ntiles) issue(tile, smem);
+    cp_async_commit();
+    for (int it = 0; tile < ntiles; ++it, tile += gridDim.x) {
+        float2* cur = smem + (it & 1) * (G::K * G::LPAD);
+        float2* nxt = smem + ((it & 1) ^ 1) * (G::K * G::LPAD);
+        if (tile + gridDim.x < ntiles) issue(tile + gridDim.x, nxt);
+        cp_async_commit();
+        cp_async_wait1();  // this tile's copies have landed (the next tile's may be in flight)
+        if (LMAP == 1) __syncthreads();
+
+        const int64_t f = tile * G::K + cl;
+        const bool active = f < a.nsub;
+        const int64_t o = f >> a.inner_log2, c = f & imask;
+        if (SMAP != 0 && t == 0) {
+            const int64_t cout = a.out_base_bits ? (int64_t)brev_bits((uint32_t)c, a.out_base_bits) : c;
+            sbase[cl] = active ? o * a.out_outer + cout * a.out_inner : -1;
+        }
+        const uint32_t cmul32 = (uint32_t)c * (uint32_t)a.tw_mul;
+        float2* region = cur + cl * G::LPAD;
+        float2 v[G::E];
 #pragma unroll
         for (int m = 0; m < G::E; ++m) {
             const int e = t + m * G::TF;
-            const int pe = a.in_elem_bitrev ? (int)brev_bits((uint32_t)e, LOG2L) : e;
-            float2 val = active ? __ldg(src + (int64_t)pe * a.in_stride) : make_float2(0.f, 0.f);
-            if (a.conj_in) val = cconj(val);
-            if (a.tw_mode == 1) val = cmul(val, tw_two_level(a.tw, (uint64_t)e * (uint64_t)c * (uint64_t)a.tw_mul));
+            float2 val = region[pad16(e)];
+            if (a.conj_in) val.y = -val.y;
+            if (a.tw_mode == 1) val = cmul(val, tw_two_level(a.tw, (uint32_t)e * cmul32));
             v[m] = val;
         }
-    }
+        if (G::NP > 1 || SMAP != 0) __syncthreads();  // buffer becomes the exchange area
 
-    stockham_passes<LOG2L, 0, G::E, G::TF>(v, t, region);
+        stockham_passes<LOG2L, 0, G::E, G::TF>(v, t, region);
 
 #pragma unroll
-    for (int m = 0; m < G::E; ++m) {
-        const int k = t + m * G::TF;
-        float2 val = v[m];
-        if (a.tw_mode == 2) val = cmul(val, tw_two_level(a.tw, (uint64_t)k * (uint64_t)c * (uint64_t)a.tw_mul));
-        if (a.conj_out) val = cconj(val);
-        if (a.scale != 1.0f) val = cscale(val, a.scale);
-        v[m] = val;
-    }
+        for (int m = 0; m < G::E; ++m) {
+            const int k = t + m * G::TF;
+            float2 val = v[m];
+            if (a.tw_mode == 2) val = cmul(val, tw_two_level(a.tw, (uint32_t)k * cmul32));
+            v[m] = make_float2(val.x * osr, val.y * osi);
+        }
 
-    if constexpr (!STORE_T) {
-        if (active) {
-            const int64_t cout = a.out_base_bits ? (int64_t)brev_bits((uint32_t)c, a.out_base_bits) : c;
-            float2* dst = out + o * a.out_outer + cout * a.out_inner;
+        if constexpr (SMAP == 0) {
+            if (active) {
+                const int64_t cout = a.out_base_bits ? (int64_t)brev_bits((uint32_t)c, a.out_base_bits) : c;
+                float2* dst = out + o * a.out_outer + cout * a.out_inner;
 #pragma unroll
-            for (int m = 0; m < G::E; ++m) {
-                const int k = t + m * G::TF;
-                const int pk = a.out_elem_bitrev ? (int)brev_bits((uint32_t)k, LOG2L) : k;
-                dst[(int64_t)pk * a.out_stride] = v[m];
+                for (int m = 0; m < G::E; ++m) {
+                    const uint32_t k = (uint32_t)(t + m * G::TF);
+                    const uint32_t pk = a.out_elem_bitrev ? brev_bits(k, LOG2L) : k;
+                    dst[pk * out_stride] = v[m];
+                }
+            }
+        } else {
+#pragma unroll
+            for (int m = 0; m < G::E; ++m) region[pad16(t + m * G::TF)] = v[m];
+            __syncthreads();
+#pragma unroll
+            for (int i = 0; i < G::E; ++i) {
+                const int idx = tid + i * G::THREADS;
+                const int cl2 = SMAP == 1 ? idx >> LOG2L : idx % G::K;
+                const uint32_t k = SMAP == 1 ? (uint32_t)(idx & (G::L - 1)) : (uint32_t)(idx / G::K);
+                const int64_t base = sbase[cl2];
+                if (base >= 0) {
+                    const uint32_t pk = a.out_elem_bitrev ? brev_bits(k, LOG2L) : k;
+                    out[base + pk * out_stride] = cur[cl2 * G::LPAD + pad16((int)k)];
+                }
             }
         }
-    } else {
-        // Stage through shared memory, then store with the opposite thread
-        // layout: element index fastest after a column-layout compute (a
-        // contiguous output row per sub-FFT), sub-FFT index fastest after a
-        // row-layout compute (coalesced when out_inner == 1).
-#pragma unroll
-        for (int m = 0; m < G::E; ++m) region[pad16(t + m * G::TF)] = v[m];
-        __syncthreads();
-#pragma unroll
-        for (int i = 0; i < G::E; ++i) {
-            const int idx = tid + i * G::THREADS;
-            const int cl2 = LAYOUT ? idx / G::L : idx % G::K;
-            const int k = LAYOUT ? idx % G::L : idx / G::K;
-            const int64_t f2 = (int64_t)blockIdx.x * G::K + cl2;
-            if (f2 < a.nsub) {
-                const int64_t o2 = f2 / a.inner, c2 = f2 - o2 * a.inner;
-                const int64_t cout = a.out_base_bits ? (int64_t)brev_bits((uint32_t)c2, a.out_base_bits) : c2;
-                const int pk = a.out_elem_bitrev ? (int)brev_bits((uint32_t)k, LOG2L) : k;
-                out[o2 * a.out_outer + cout * a.out_inner + (int64_t)pk * a.out_stride] =
-                    smem[cl2 * G::LPAD + pad16(k)];
-            }
-        }
+        __syncthreads();  // `cur` is refilled two tiles from now
     }
 }
 
-template <int LOG2L, int LAYOUT, int STORE_T>
+static int g_num_sms = 0;
+
+template <int LOG2L, int LAYOUT, int LMAP, int SMAP>
 static cudaError_t launch_pass_t(const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
-    using G = PassGeo<LOG2L, LAYOUT, STORE_T>;
-    const size_t smem = G::SMEM ? (size_t)G::K * G::LPAD * sizeof(float2) : 0;
-    auto kern = k_pass<LOG2L, LAYOUT, STORE_T>;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    using G = PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>;
+    auto kern = k_pass<LOG2L, LAYOUT, LMAP, SMAP>;
+    static int blocks_per_sm[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (blocks_per_sm[dev] == 0) {
+        if (G::SMEM > 48 * 1024) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::SMEM);
+            if (e != cudaSuccess) return e;
+        }
+        int nb = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, G::THREADS, G::SMEM);
         if (e != cudaSuccess) return e;
+        if (g_num_sms == 0) {
+            e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess) return e;
+        }
+        blocks_per_sm[dev] = nb > 0 ? nb : 1;
     }
-    const int64_t ctas = (a.nsub + G::K - 1) / G::K;
-    if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-    kern<<<(unsigned)ctas, G::THREADS, smem, s>>>(in, out, a);
+    const int64_t ntiles = (a.nsub + G::K - 1) / G::K;
+    int64_t grid = (int64_t)blocks_per_sm[dev] * g_num_sms;
+    if (grid > ntiles) grid = ntiles;
+    if (grid < 1) grid = 1;
+    kern<<<(unsigned)grid, G::THREADS, G::SMEM, s>>>(in, out, a);
     return cudaGetLastError();
 }
 
 template <int LOG2L>
-static cudaError_t launch_pass_l(int layout, int store_t, const float2* in, float2* out,
+static cudaError_t launch_pass_l(int layout, int lmap, int smap, const float2* in, float2* out,
                                  const PassArgs& a, cudaStream_t s) {
-    if (layout) {
-        return store_t ? launch_pass_t<LOG2L, 1, 1>(in, out, a, s) : launch_pass_t<LOG2L, 1, 0>(in, out, a, s);
+    if (layout) {  // columns: per-thread loads, stores direct or staged element-fastest
+        return smap == 1 ? launch_pass_t<LOG2L, 1, 0, 1>(in, out, a, s) : launch_pass_t<LOG2L, 1, 0, 0>(in, out, a, s);
     }
-    return store_t ? launch_pass_t<LOG2L, 0, 1>(in, out, a, s) : launch_pass_t<LOG2L, 0, 0>(in, out, a, s);
+    if (lmap) {
+        return smap == 2 ? launch_pass_t<LOG2L, 0, 1, 2>(in, out, a, s)
+             : smap == 1 ? launch_pass_t<LOG2L, 0, 1, 1>(in, out, a, s)
+                         : launch_pass_t<LOG2L, 0, 1, 0>(in, out, a, s);
+    }
+    return smap == 2 ? launch_pass_t<LOG2L, 0, 0, 2>(in, out, a, s)
+         : smap == 1 ? launch_pass_t<LOG2L, 0, 0, 1>(in, out, a, s)
+                     : launch_pass_t<LOG2L, 0, 0, 0>(in, out, a, s);
 }
 
-cudaError_t launch_pass(int log2l, int layout, int store_t, const float2* in, float2* out,
+cudaError_t launch_pass(int log2l, int layout, int lmap, int smap, const float2* in, float2* out,
                         const PassArgs& a, cudaStream_t s) {
     switch (log2l) {
-        case 1: return launch_pass_l<1>(layout, store_t, in, out, a, s);
-        case 2: return launch_pass_l<2>(layout, store_t, in, out, a, s);
-        case 3: return launch_pass_l<3>(layout, store_t, in, out, a, s);
-        case 4: return launch_pass_l<4>(layout, store_t, in, out, a, s);
-        case 5: return launch_pass_l<5>(layout, store_t, in, out, a, s);
-        case 6: return launch_pass_l<6>(layout, store_t, in, out, a, s);
-        case 7: return launch_pass_l<7>(layout, store_t, in, out, a, s);
-        case 8: return launch_pass_l<8>(layout, store_t, in, out, a, s);
-        case 9: return launch_pass_l<9>(layout, store_t, in, out, a, s);
-        case 10: return launch_pass_l<10>(layout, store_t, in, out, a, s);
-        case 11: return launch_pass_l<11>(layout, store_t, in, out, a, s);
-        case 12: return launch_pass_l<12>(layout, store_t, in, out, a, s);
+        case 1: return launch_pass_l<1>(layout, lmap, smap, in, out, a, s);
+        case 2: return launch_pass_l<2>(layout, lmap, smap, in, out, a, s);
+        case 3: return launch_pass_l<3>(layout, lmap, smap, in, out, a, s);
+        case 4: return launch_pass_l<4>(layout, lmap, smap, in, out, a, s);
+        case 5: return launch_pass_l<5>(layout, lmap, smap, in, out, a, s);
+        case 6: return launch_pass_l<6>(layout, lmap, smap, in, out, a, s);
+        case 7: return launch_pass_l<7>(layout, lmap, smap, in, out, a, s);
+        case 8: return launch_pass_l<8>(layout, lmap, smap, in, out, a, s);
+        case 9: return launch_pass_l<9>(layout, lmap, smap, in, out, a, s);
+        case 10: return launch_pass_l<10>(layout, lmap, smap, in, out, a, s);
+        case 11: return launch_pass_l<11>(layout, lmap, smap, in, out, a, s);
+        case 12: return launch_pass_l<12>(layout, lmap, smap, in, out, a, s);
         default: return cudaErrorInvalidValue;
     }
 }

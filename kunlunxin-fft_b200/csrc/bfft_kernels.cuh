@@ -72,7 +72,8 @@ cudaError_t launch_scale(const float2* x, float2* y, int64_t count, float scale,
 // or post (output k times W_N^{k*c*tw_mul}) with the plan's two-level W_N.
 struct PassArgs {
     int64_t nsub;
-    int64_t inner;
+    int64_t inner;       // a power of two
+    int inner_log2;
     int64_t in_outer, in_inner, in_stride;
     int64_t out_outer, out_inner, out_stride;
     int in_base_bits, out_base_bits;
@@ -88,9 +89,11 @@ struct PassArgs {
 constexpr int kMaxPassLog2 = 12;  // largest CTA-resident sub-FFT: 4096 points
 
 // layout: 0 rows (element index fastest across threads), 1 columns (sub-FFT
-// index fastest).  store_t: stage the final store through shared memory so the
-// store is coalesced along the sub-FFT index.
-cudaError_t launch_pass(int log2l, int layout, int store_t, const float2* in, float2* out,
+// index fastest).  lmap: 1 = the tile is contiguous and is copied
+// cooperatively (rows only).  smap: 0 store from registers, 1 staged store
+// with the element index fastest, 2 staged store with the sub-FFT index
+// fastest (rows only).
+cudaError_t launch_pass(int log2l, int layout, int lmap, int smap, const float2* in, float2* out,
                         const PassArgs& a, cudaStream_t s);
 
 }  // namespace bfft

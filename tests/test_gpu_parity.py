@@ -317,7 +317,7 @@ def test_sweep_config_full_size_properties():
         back = execute_fft_plan(inv, y)
         err = (torch.linalg.vector_norm(back - x) / torch.linalg.vector_norm(x)).item()
         assert err <= 2 * TOL_F64, (n, err)
-        pars = (torch.linalg.vector_norm(y.double()) ** 2 / n / torch.linalg.vector_norm(x.double()) ** 2).item()
+        pars = (torch.linalg.vector_norm(y.to(torch.complex128)) ** 2 / n / torch.linalg.vector_norm(x.to(torch.complex128)) ** 2).item()
         assert abs(pars - 1) < 1e-5, (n, pars)
         y2 = execute_fft_plan(fwd, 2 * x + 0.5j * x)
         lin = (torch.linalg.vector_norm(y2 - (2 + 0.5j) * y) / torch.linalg.vector_norm(y2)).item()
