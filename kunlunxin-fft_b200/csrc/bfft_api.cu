@@ -160,8 +160,10 @@ Step pass_step(int log2l, int layout, int transpose_store, const PassArgs& pa) {
     const int64_t tf = L < 16 ? 1 : L / 16;
     s.smap = transpose_store ? (layout ? 1 : 2) : 0;
     if (!layout) {
+        // sub-FFT f = o*inner + c starts at f*L  <=>  in_outer = inner*L and
+        // (in_inner = L or a single sub-FFT per outer index)
         const bool contiguous_in = pa.in_stride == 1 && !pa.in_elem_bitrev && !pa.in_base_bits &&
-                                   pa.in_inner == L && pa.in_outer == pa.inner * L;
+                                   pa.in_outer == pa.inner * L && (pa.inner == 1 || pa.in_inner == L);
         s.lmap = contiguous_in ? 1 : 0;
         if (s.smap == 0 && tf < 32 && pa.out_stride == 1 && !pa.out_elem_bitrev) s.smap = 1;
     }

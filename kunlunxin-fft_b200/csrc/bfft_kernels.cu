@@ -529,7 +529,7 @@ struct PassKGeo {
     static constexpr int L = 1 << LOG2L;
     static constexpr int E = L < 16 ? L : 16;
     static constexpr int TF = L / E;
-    static constexpr int LPAD = L + (L >> 4) + 1;
+    static constexpr int LPAD = (L + (L >> 4)) | 1;  // odd: regions start on distinct banks
     // sub-FFTs per CTA: ~256 threads; >= 4 when the sub-FFT index is the
     // coalesced dimension; capped so two tile buffers fit in 200 KB.
     static constexpr int KMIN = (LAYOUT || SMAP == 2) ? 4 : 1;
