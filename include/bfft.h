@@ -159,6 +159,31 @@ BFFT_EXPORT bfft_status bfft_twiddle_table(void* w, int64_t n, int64_t count, in
  * 1 DIT radix-4 digit reversal (:41-57), 2 DIF digit reversal (:60-78). */
 BFFT_EXPORT bfft_status bfft_index_map(int32_t kind, int32_t bits, void* out, int32_t device, void* stream);
 
+/* 4-step C2C without any device allocation -- no counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory while they run: code inside
+ * another framework's fixed memory pool, loops where cudaMalloc / cudaFree
+ * would synchronise the device, or an FFI host with no allocator for the CUDA
+ * context.  Same transform as a run_hybrid plan through bfft_execute (x is
+ * (batch, n) complex64, n = (n / tile) * tile with both factors <= 4096,
+ * transform_direction / norm as in bfft_plan_desc), but the scratch buffer of
+ * the two passes is a fixed device array inside this library.
+ *   - Limit: batch * n <= BFFT_NOALLOC_MAX_ELEMS (2^22 complex64 = 32 MiB);
+ *     larger requests return BFFT_ERR_SHAPE.  Every GPU that loads the library
+ *     holds that array (and a 32 KiB twiddle table) until the process exits.
+ *   - No cudaMalloc / cudaFree or other allocating call is made.  The first
+ *     call on a device sets up that device (looks up the arrays' device
+ *     addresses, fills the library's unit twiddle tables and synchronises the
+ *     legacy default stream once); make that first call before any stream
+ *     capture.
+ *   - All calls share the array and it keeps the last call's contents; calls
+ *     whose executions overlap on the GPU race -- serialise them on one
+ *     stream. */
+#define BFFT_NOALLOC_MAX_ELEMS (1LL << 22)
+BFFT_EXPORT bfft_status bfft_hybrid_c2c_noalloc(const void* in, void* out, int64_t n, int64_t batch,
+                                                int64_t tile, int32_t transform_direction, int32_t norm,
+                                                int32_t device, void* stream);
+
 /* Total kernels this library has enqueued in this process (all devices). */
 BFFT_EXPORT uint64_t bfft_launch_counter(void);
 

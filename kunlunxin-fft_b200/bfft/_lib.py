@@ -29,7 +29,7 @@ VARIANT_IDS = {"spread": 0, "folded": 1}
 EXPORTS = ("bfft_api_version", "bfft_last_error", "bfft_plan_create", "bfft_plan_workspace_size",
            "bfft_plan_launches", "bfft_execute", "bfft_plan_destroy", "bfft_bit_reverse_permute",
            "bfft_r2c_stitch", "bfft_c2r_pre", "bfft_c2r_unpack", "bfft_twiddle_table",
-           "bfft_index_map", "bfft_launch_counter")
+           "bfft_index_map", "bfft_launch_counter", "bfft_hybrid_c2c_noalloc")
 
 
 class PlanDesc(ctypes.Structure):
@@ -80,6 +80,7 @@ def load() -> ctypes.CDLL:
         L.bfft_c2r_unpack.argtypes = [vp, vp, i64, i64, ctypes.c_float, i32, vp]
         L.bfft_twiddle_table.argtypes = [vp, i64, i64, i32, vp]
         L.bfft_index_map.argtypes = [i32, i32, vp, i32, vp]
+        L.bfft_hybrid_c2c_noalloc.argtypes = [vp, vp, i64, i64, i64, i32, i32, i32, vp]
         for name in EXPORTS:
             fn = getattr(L, name)
             if name not in ("bfft_api_version", "bfft_last_error", "bfft_launch_counter"):

@@ -516,6 +516,12 @@ cudaError_t run_core(const std::vector<Step>& st, const float2* src, float2* dst
 
 }  // namespace
 
+// Shared with the other translation units of the library (bfft_noalloc.cu).
+namespace bfft {
+void set_last_error(const char* msg) { g_last_error = msg; }
+void count_launches(int k) { g_launches.fetch_add((uint64_t)k, std::memory_order_relaxed); }
+}  // namespace bfft
+
 // ================================================================ C ABI
 
 extern "C" {

@@ -50,6 +50,10 @@ cudaError_t launch_real_part(const float2* y, float* out, int64_t total, float s
 cudaError_t launch_twiddle_table(float2* w, int64_t n, int64_t count, cudaStream_t s);
 cudaError_t launch_index_map(int kind, int bits, uint32_t* out, cudaStream_t s);
 
+// Library-wide error message (bfft_last_error) and launch counter.
+void set_last_error(const char* msg);
+void count_launches(int k);
+
 // Real-transform epilogues (standalone forms of the reference runner API).
 cudaError_t launch_r2c_stitch(const float2* z, float2* x, int64_t n, int64_t batch, float scale,
                               TwoLevel twn, cudaStream_t s);
