@@ -75,7 +75,7 @@ class ClockSampler:
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.gpu)], stdout=self.file,
+                                          "-lms", "20", "-i", str(self.gpu)], stdout=self.file,
                                          stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
