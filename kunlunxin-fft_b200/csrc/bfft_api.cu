@@ -70,13 +70,14 @@ double norm_scale(int64_t n, int tdir, int norm) {
     return 1.0;
 }
 
-enum StepKind { S_STAGE2, S_STAGE4, S_PASS, S_BITREV, S_SCALE };
+enum StepKind { S_STAGE2, S_STAGE4, S_PASS, S_CLUSTER };
 
 struct Step {
     StepKind kind;
     bool dif = false;
     StageArgs st{};
     PassArgs pa{};
+    ClusterArgs ca{};
     int log2l = 0, layout = 0, lmap = 0, smap = 0;
     int block = 256;
 };
@@ -373,8 +374,22 @@ bfft_status build_core(bfft_plan_s& P) {
                 return BFFT_OK;
             }
             const int lt = tile_log2(d.tile, 64);
-            if (lt > kMaxPassLog2)
-                return fail(BFFT_ERR_UNSUPPORTED, "matrix tile 2^%d exceeds the CTA-resident limit 2^%d", lt, kMaxPassLog2);
+            if (lt > kMaxPassLog2) {
+                // A local group of the whole transform beyond one CTA: the
+                // cluster kernel holds all N points on chip across its CTAs.
+                if (lt == log2n && cluster_supported(log2n)) {
+                    Step c;
+                    c.kind = S_CLUSTER;
+                    c.log2l = log2n;
+                    c.ca.batch = B;
+                    c.ca.tw = tw;
+                    c.ca.scale = 1.0f;
+                    st.push_back(c);
+                    return BFFT_OK;
+                }
+                return fail(BFFT_ERR_UNSUPPORTED, "matrix tile 2^%d exceeds the on-chip limit (2^%d per CTA, "
+                            "whole transforms of 2^13..2^16 per cluster)", lt, kMaxPassLog2);
+            }
             std::vector<int> parts = split_stages(log2n - lt);
             if (!dif) {
                 st.push_back(dit_local(n, B, lt, tw));
@@ -476,6 +491,7 @@ bfft_status build_core(bfft_plan_s& P) {
 void set_first_conj(std::vector<Step>& st) {
     Step& s = st.front();
     if (s.kind == S_PASS) s.pa.conj_in = 1;
+    else if (s.kind == S_CLUSTER) s.ca.conj_in = 1;
     else s.st.conj_in = 1;
 }
 void set_last_epilogue(std::vector<Step>& st, int conj, float scale) {
@@ -483,6 +499,9 @@ void set_last_epilogue(std::vector<Step>& st, int conj, float scale) {
     if (s.kind == S_PASS) {
         s.pa.conj_out = conj;
         s.pa.scale = scale;
+    } else if (s.kind == S_CLUSTER) {
+        s.ca.conj_out = conj;
+        s.ca.scale = scale;
     } else {
         s.st.conj_out = conj;
         s.st.scale = scale;
@@ -495,6 +514,7 @@ cudaError_t launch_step(const Step& s, const float2* in, float2* out, cudaStream
         case S_STAGE2: return launch_radix2_stage(s.dif, in, out, s.st, s.block, stream);
         case S_STAGE4: return launch_radix4_stage(s.dif, in, out, s.st, s.block, stream);
         case S_PASS: return launch_pass(s.log2l, s.layout, s.lmap, s.smap, in, out, s.pa, stream);
+        case S_CLUSTER: return launch_cluster_fft(s.log2l, in, out, s.ca, stream);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -11,6 +11,7 @@
 //     stored once.  One pass is a complete FFT for N <= 4096; larger N and the
 //     reference's local-group / grouped-tail / 4-step flows are sequences of
 //     such passes with fused twiddles.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -455,8 +456,39 @@ __host__ __device__ constexpr int radix_log2(int log2l, int pass) { return pass 
 // runs an R-point DFT and sends output j to (b/p) p R + (b mod p) + j p.
 // Thread t owns elements t + m' TF (m' < E), so butterfly q of the thread
 // reads and writes slots q + j (E/R).
+// Shared-memory twiddle tables of one sub-FFT length: for every pass with
+// p > 1, rows k < p of R-1 entries W_{Rp}^{j k} (j = 1..R-1).  The odd row
+// stride R-1 keeps consecutive k on distinct banks; a thread's row depends
+// only on its index, so a persistent CTA fills the tables once.
+__host__ __device__ constexpr int tw_pass_entries(int log2l, int pass) {
+    return pass == 0 ? 0 : (1 << (4 * pass)) * ((1 << radix_log2(log2l, pass)) - 1);
+}
+__host__ __device__ constexpr int tw_offset(int log2l, int pass) {
+    int off = 0;
+    for (int p = 1; p < pass; ++p) off += tw_pass_entries(log2l, p);
+    return off;
+}
+__host__ __device__ constexpr int tw_total(int log2l) {
+    return log2l <= 4 ? 0 : tw_offset(log2l, (log2l + 3) / 4);
+}
+
+template <int LOG2L>
+__device__ __forceinline__ void fill_stockham_twiddles(float2* tw_smem) {
+    constexpr int NP = LOG2L <= 4 ? 1 : (LOG2L + 3) / 4;
+    for (int pass = 1; pass < NP; ++pass) {
+        const int r = 1 << radix_log2(LOG2L, pass), p = 1 << (4 * pass);
+        const float2* lvl = g_tw_levels + r * p;
+        float2* dst = tw_smem + tw_offset(LOG2L, pass);
+        const int cnt = p * (r - 1);
+        for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+            const int k = i / (r - 1), j = i - k * (r - 1) + 1;
+            dst[i] = lvl[j * k];
+        }
+    }
+}
+
 template <int LOG2L, int PASS, int E, int TF>
-__device__ __forceinline__ void stockham_passes(float2 (&v)[E], int t, float2* region) {
+__device__ __forceinline__ void stockham_passes(float2 (&v)[E], int t, float2* region, const float2* tw_smem) {
     constexpr int NP = LOG2L <= 4 ? 1 : (LOG2L + 3) / 4;
     if constexpr (PASS < NP) {
         constexpr int LR = radix_log2(LOG2L, PASS);
@@ -471,9 +503,9 @@ __device__ __forceinline__ void stockham_passes(float2 (&v)[E], int t, float2* r
 #pragma unroll
             for (int j = 0; j < R; ++j) u[j] = v[q + j * NB];
             if constexpr (PASS > 0) {
-                const float2* tw = g_tw_levels + (R << LP);
+                const float2* tw = tw_smem + tw_offset(LOG2L, PASS) + k * (R - 1) - 1;
 #pragma unroll
-                for (int j = 1; j < R; ++j) u[j] = cmul(u[j], __ldg(tw + j * k));
+                for (int j = 1; j < R; ++j) u[j] = cmul(u[j], tw[j]);
             }
             Dft<R>::run(u);
 #pragma unroll
@@ -492,7 +524,7 @@ __device__ __forceinline__ void stockham_passes(float2 (&v)[E], int t, float2* r
 #pragma unroll
             for (int m = 0; m < E; ++m) v[m] = region[pad16(t + m * TF)];
             __syncthreads();
-            stockham_passes<LOG2L, PASS + 1, E, TF>(v, t, region);
+            stockham_passes<LOG2L, PASS + 1, E, TF>(v, t, region, tw_smem);
         }
     }
 }
@@ -541,7 +573,8 @@ struct PassKGeo {
     // resident CTAs the register budget is sized for (~768 threads per SM)
     static constexpr int MINB = THREADS >= 768 ? 1 : 768 / THREADS;
     static constexpr int NP = LOG2L <= 4 ? 1 : (LOG2L + 3) / 4;
-    static constexpr size_t SMEM = (size_t)2 * K * LPAD * sizeof(float2) + (size_t)K * sizeof(int64_t);
+    static constexpr size_t SMEM = (size_t)2 * K * LPAD * sizeof(float2) + (size_t)K * sizeof(int64_t) +
+                                   (size_t)tw_total(LOG2L) * sizeof(float2);
 };
 
 template <int LOG2L, int LAYOUT, int LMAP, int SMAP>
@@ -551,6 +584,8 @@ __global__ void __launch_bounds__(PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>::THREADS,
     using G = PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>;
     extern __shared__ __align__(16) float2 smem[];
     int64_t* sbase = reinterpret_cast<int64_t*>(smem + 2 * G::K * G::LPAD);
+    float2* tw_smem = reinterpret_cast<float2*>(sbase + G::K);
+    fill_stockham_twiddles<LOG2L>(tw_smem);  // visible after the first in-loop barrier
     const int tid = threadIdx.x;
     const int cl = LAYOUT ? tid % G::K : tid / G::TF;
     const int t = LAYOUT ? tid / G::K : tid % G::TF;
@@ -616,7 +651,7 @@ __global__ void __launch_bounds__(PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>::THREADS,
         }
         if (G::NP > 1 || SMAP != 0) __syncthreads();  // buffer becomes the exchange area
 
-        stockham_passes<LOG2L, 0, G::E, G::TF>(v, t, region);
+        stockham_passes<LOG2L, 0, G::E, G::TF>(v, t, region, tw_smem);
 
 #pragma unroll
         for (int m = 0; m < G::E; ++m) {
@@ -721,6 +756,187 @@ cudaError_t launch_pass(int log2l, int layout, int lmap, int smap, const float2*
         case 10: return launch_pass_l<10>(layout, lmap, smap, in, out, a, s);
         case 11: return launch_pass_l<11>(layout, lmap, smap, in, out, a, s);
         case 12: return launch_pass_l<12>(layout, lmap, smap, in, out, a, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// ============================================================== cluster FFT
+//
+// One HBM round trip for 4096 < N <= 65536: the 4-step N = N1 * N2 runs on a
+// thread-block cluster of P CTAs.  CTA r of the cluster owns columns
+// n2 in [r*N2/P, (r+1)*N2/P) for the N1-point column FFTs (stride-N2 loads,
+// coalesced across its columns), multiplies by W_N^{n2 k1} and leaves the
+// result in its shared memory; after a cluster barrier every CTA gathers its
+// rows k1 in [r*N1/P, (r+1)*N1/P) from all P CTAs through distributed shared
+// memory, runs the N2-point row FFTs and stores X[k1 + N1 k2] (staged so the
+// store is coalesced across its rows).  Persistent over the batch: the next
+// transform's columns are copied in with cp.async while the current one is
+// gathered, transformed and stored.  Synchronisation is the hardware cluster
+// barrier only (every CTA runs the same iterations), and a final barrier keeps
+// each CTA's shared memory alive until the others have finished reading it.
+template <int LOG2N1, int LOG2N2, int LOG2P>
+struct CluGeo {
+    static constexpr int N1 = 1 << LOG2N1, N2 = 1 << LOG2N2, P = 1 << LOG2P;
+    static constexpr int64_t N = (int64_t)N1 * N2;
+    static constexpr int LOG2CA = LOG2N2 - LOG2P;
+    static constexpr int CA = N2 / P;  // pass-A columns per CTA
+    static constexpr int RB = N1 / P;  // pass-B rows per CTA
+    static constexpr int M = N1 * N2 / P;
+    static constexpr int E = 16;
+    static constexpr int TFA = N1 / E, TFB = N2 / E;
+    static constexpr int THREADS = M / E;
+    static constexpr int MINB = THREADS >= 768 ? 1 : 768 / THREADS;
+    static constexpr int LPADA = (N1 + (N1 >> 4)) | 1;
+    static constexpr int LPADB = (N2 + (N2 >> 4)) | 1;
+    static constexpr int XSZ = CA * LPADA;
+    static constexpr int YSZ = M > RB * LPADB ? M : RB * LPADB;
+    static constexpr int TWA = tw_total(LOG2N1), TWB = tw_total(LOG2N2);
+    static constexpr size_t SMEM = (size_t)(XSZ + YSZ + TWA + TWB) * sizeof(float2);
+};
+
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+template <int LOG2N1, int LOG2N2, int LOG2P>
+__global__ void __launch_bounds__(CluGeo<LOG2N1, LOG2N2, LOG2P>::THREADS, CluGeo<LOG2N1, LOG2N2, LOG2P>::MINB)
+    k_cluster_fft(const float2* __restrict__ in, float2* __restrict__ out, ClusterArgs a) {
+    using G = CluGeo<LOG2N1, LOG2N2, LOG2P>;
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    extern __shared__ __align__(16) float2 smem[];
+    float2* X = smem;
+    float2* Y = smem + G::XSZ;
+    float2* twA = Y + G::YSZ;
+    float2* twB = twA + G::TWA;
+    fill_stockham_twiddles<LOG2N1>(twA);  // visible after the first in-loop barrier
+    fill_stockham_twiddles<LOG2N2>(twB);
+    const int rank = (int)cluster.block_rank();
+    const int64_t cid = blockIdx.x / G::P;
+    const int64_t nclu = gridDim.x / G::P;
+    const int tid = threadIdx.x;
+    const int clA = tid % G::CA, tA = tid / G::CA;    // pass A: column fastest
+    const int rlB = tid / G::TFB, tB = tid % G::TFB;  // pass B: element fastest
+    const int n2 = rank * G::CA + clA;
+    const int k1 = rank * G::RB + rlB;
+    float2* regA = X + clA * G::LPADA;
+    float2* regB = Y + rlB * G::LPADB;
+    const float osr = a.scale, osi = a.conj_out ? -a.scale : a.scale;
+
+    auto issue = [&](int64_t b) {
+        const float2* src = in + b * G::N + n2;
+#pragma unroll
+        for (int m = 0; m < G::E; ++m) {
+            const int e = tA + m * G::TFA;
+            cp_async8(regA + pad16(e), src + (int64_t)e * G::N2);
+        }
+    };
+
+    int64_t b = cid;
+    if (b < a.batch) issue(b);
+    cp_async_commit();
+    for (; b < a.batch; b += nclu) {
+        cp_async_wait0();
+        float2 v[G::E];
+#pragma unroll
+        for (int m = 0; m < G::E; ++m) {
+            float2 val = regA[pad16(tA + m * G::TFA)];
+            if (a.conj_in) val.y = -val.y;
+            v[m] = val;
+        }
+        __syncthreads();
+        stockham_passes<LOG2N1, 0, G::E, G::TFA>(v, tA, regA, twA);
+#pragma unroll
+        for (int m = 0; m < G::E; ++m) {
+            const int k = tA + m * G::TFA;
+            Y[k * G::CA + clA] = cmul(v[m], tw_two_level(a.tw, (uint32_t)(n2 * k)));
+        }
+        cluster.sync();  // every CTA's twiddled columns are in place
+        if (b + nclu < a.batch) issue(b + nclu);
+        cp_async_commit();
+#pragma unroll
+        for (int m = 0; m < G::E; ++m) {
+            const int n = tB + m * G::TFB;
+            const float2* rp = cluster.map_shared_rank(Y + (k1 * G::CA + (n & (G::CA - 1))), n >> G::LOG2CA);
+            v[m] = *rp;
+        }
+        cluster.sync();  // all remote reads of Y are done
+        stockham_passes<LOG2N2, 0, G::E, G::TFB>(v, tB, regB, twB);
+#pragma unroll
+        for (int m = 0; m < G::E; ++m) regB[pad16(tB + m * G::TFB)] = make_float2(v[m].x * osr, v[m].y * osi);
+        __syncthreads();
+        float2* dst = out + b * G::N + rank * G::RB;
+#pragma unroll
+        for (int i = 0; i < G::E; ++i) {
+            const int idx = tid + i * G::THREADS;
+            const int rl2 = idx % G::RB, k2 = idx / G::RB;
+            dst[rl2 + (int64_t)G::N1 * k2] = Y[rl2 * G::LPADB + pad16(k2)];
+        }
+        __syncthreads();
+    }
+    cluster.sync();
+}
+
+template <int LOG2N1, int LOG2N2, int LOG2P>
+static cudaError_t launch_cluster_t(const float2* in, float2* out, const ClusterArgs& a, cudaStream_t s) {
+    using G = CluGeo<LOG2N1, LOG2N2, LOG2P>;
+    auto kern = k_cluster_fft<LOG2N1, LOG2N2, LOG2P>;
+    static int max_clusters[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = G::P;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(G::THREADS);
+    cfg.dynamicSmemBytes = G::SMEM;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (max_clusters[dev] == 0) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::SMEM);
+        if (e != cudaSuccess) return e;
+        if (G::P > 8) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return e;
+        }
+        int sms = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        cfg.gridDim = dim3((unsigned)(G::P * sms));
+        int nc = 0;
+        e = cudaOccupancyMaxActiveClusters(&nc, kern, &cfg);
+        if (e != cudaSuccess) return e;
+        max_clusters[dev] = nc > 0 ? nc : 1;
+    }
+    int64_t nclu = max_clusters[dev];
+    if (nclu > a.batch) nclu = a.batch;
+    cfg.gridDim = dim3((unsigned)(nclu * G::P));
+    e = cudaLaunchKernelEx(&cfg, kern, in, out, a);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+bool cluster_supported(int log2n) { return log2n >= 13 && log2n <= 16; }
+
+cudaError_t launch_cluster_fft(int log2n, const float2* in, float2* out, const ClusterArgs& a, cudaStream_t s) {
+    switch (log2n) {
+        case 13: return launch_cluster_t<6, 7, 1>(in, out, a, s);
+        case 14: return launch_cluster_t<7, 7, 2>(in, out, a, s);
+        case 15: return launch_cluster_t<7, 8, 3>(in, out, a, s);
+        case 16: {
+            // 16-CTA clusters (non-portable size) keep 4096 points per CTA and
+            // three CTAs per SM; fall back to portable 8-CTA clusters.
+            cudaError_t e = launch_cluster_t<8, 8, 4>(in, out, a, s);
+            if (e == cudaErrorInvalidValue || e == cudaErrorInvalidConfiguration ||
+                e == cudaErrorNotSupported || e == cudaErrorInvalidClusterSize) {
+                (void)cudaGetLastError();
+                e = launch_cluster_t<8, 8, 3>(in, out, a, s);
+            }
+            return e;
+        }
         default: return cudaErrorInvalidValue;
     }
 }

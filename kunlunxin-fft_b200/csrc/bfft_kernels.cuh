@@ -50,6 +50,19 @@ cudaError_t launch_real_part(const float2* y, float* out, int64_t total, float s
 cudaError_t launch_twiddle_table(float2* w, int64_t n, int64_t count, cudaStream_t s);
 cudaError_t launch_index_map(int kind, int bits, uint32_t* out, cudaStream_t s);
 
+// ---------------------------------------------------------------- cluster FFT
+// Whole transforms of N = 2^13 .. 2^16 points in one HBM round trip on a
+// thread-block cluster (4-step with the transpose in distributed shared
+// memory).  `tw` is the plan's W_N table.
+struct ClusterArgs {
+    int64_t batch;
+    TwoLevel tw;
+    float scale;
+    int conj_in, conj_out;
+};
+bool cluster_supported(int log2n);
+cudaError_t launch_cluster_fft(int log2n, const float2* in, float2* out, const ClusterArgs& a, cudaStream_t s);
+
 // Library-wide error message (bfft_last_error) and launch counter.
 void set_last_error(const char* msg);
 void count_launches(int k);

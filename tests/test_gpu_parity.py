@@ -342,3 +342,25 @@ def test_batch_shard_config_full_size():
                                   transform_direction="inverse"), y)
     err = (torch.linalg.vector_norm(back - x) / torch.linalg.vector_norm(x)).item()
     assert err <= 2 * TOL_F64
+
+
+@pytest.mark.parametrize("log2n", [13, 14, 15, 16])
+def test_cluster_single_pass(log2n):
+    """Whole transforms of 2^13..2^16 points in one HBM round trip (thread-block
+    cluster, transpose through distributed shared memory): M2 with tile = N."""
+    n = 1 << log2n
+    rng = np.random.default_rng(log2n)
+    for b in (1, 2, 64):
+        x = cplx(rng, (b, n))
+        t = dev(x)
+        for direction in ("dit", "dif"):
+            name = f"fft_{direction}_matrix_batch"
+            got = host(getattr(runner, name)(t, tile=n))
+            assert rel_l2_per_transform(got, _f64(x)) <= TOL_F64, (n, b, direction)
+        p = _plan("fft_dit_matrix_batch", n, b, params={"tile": n}, transform_direction="inverse", norm="ortho")
+        y = host(execute_fft_plan(p, t if b > 1 else t[0])).reshape(b, n)
+        ref = np.fft.ifft(x.astype(np.complex128), norm="ortho")
+        assert rel_l2_per_transform(y, ref) <= TOL_F64, (n, b, "inverse")
+    from bfft.entry import native_plan_for
+
+    assert native_plan_for(_plan("fft_dit_matrix_batch", n, 64, params={"tile": n}), 0).launches == 1
