@@ -40,6 +40,8 @@ WORKLOADS = {
            "desc": "config 5a: batch-sharded C2C forward, N=65536, B=8192 (4 GiB complex64) split over ranks"},
     "sweep-2^12": {"n": 4096, "batch": 4096, "desc": "config 3 point: C2C forward N=4096, B=4096 (B*N=2^24)"},
     "sweep-2^20": {"n": 1 << 20, "batch": 16, "desc": "config 3 point: C2C forward N=2^20, B=16 (B*N=2^24)"},
+    "5b": {"n": 1 << 30, "batch": 1, "kind": "4step", "cpu_n": 1 << 20,
+           "desc": "config 5b: one C2C forward of N=2^30 (8 GiB complex64); 4-step over ranks with NCCL all-to-all"},
 }
 SEED = 1234
 FALLBACK_HBM_GBS = 6650.0
@@ -154,16 +156,20 @@ def run_reference_arm(args, wl) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
+    # The reference's C++ FFT runs one transform per thread: a batched job
+    # uses every host core, one 2^30-point transform (config 5b) runs on one
+    # thread and is sampled at N = cpu_n (a full one takes minutes).
+    threads = 1 if wl.get("kind") == "4step" else (os.cpu_count() or 1)
+    n = wl.get("cpu_n", wl["n"])
     # size one step to about 2 s of wall time so K+W steps stay within minutes
-    probe = reference_cpu(wl["n"], 2.0, threads)
+    probe = reference_cpu(n, 2.0, threads)
     rows = probe["rows"]
     import numpy as np
 
     from oracle import oracle as O
 
     rng = np.random.default_rng(SEED)
-    x = (rng.standard_normal((rows, wl["n"])) + 1j * rng.standard_normal((rows, wl["n"]))).astype(np.complex128)
+    x = (rng.standard_normal((rows, n)) + 1j * rng.standard_normal((rows, n))).astype(np.complex128)
     L = O.reference_lib()
 
     def step():
@@ -178,7 +184,7 @@ def run_reference_arm(args, wl) -> None:
     for _ in range(args.steps):
         step()
     t = time.perf_counter() - t0
-    value = gflop(wl["n"], rows) * args.steps / t
+    value = gflop(n, rows) * args.steps / t
     line = {
         "impl": "reference", "metric": "complex64 C2C FFT GFLOP/s (5N*log2N/t)", "value": value,
         "unit": "GFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -186,7 +192,7 @@ def run_reference_arm(args, wl) -> None:
         "vs_baseline": None, "dtype": "complex128 (reference CPU path is float64)",
         "data": f"synthetic iid N(0,1) re/im, seed {SEED}",
         "config": {"workload": wl["desc"], "n": wl["n"], "global_batch": wl["batch"],
-                   "sample_rows_per_step": rows, "parallelism": f"{threads} host threads"},
+                   "sample_rows_per_step": rows, "sample_n": n, "parallelism": f"{threads} host threads"},
         "cpu_baseline": {"value": value, "unit": "GFLOP/s", "cores": probe["cores"], "kind": probe["kind"],
                          "sample": probe["sample"]},
         "e2e": {"value": value, "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -208,13 +214,215 @@ def choose_plan(n: int, b: int):
     if not p.fallback:
         return p, "selector"
     log2n = n.bit_length() - 1
-    tile = n if n <= 4096 else 1 << ((log2n + 1) // 2)
+    if n <= 4096:
+        tile = n
+    else:  # fewest CTA-resident passes of <= 2^12 points, as equal as possible
+        passes = -(-log2n // 12)
+        tile = 1 << -(-log2n // passes)
+    executed = "fft_dit_matrix_batch" if b > 1 else "fft_dit_matrix"
     return ExecutionPlan(n=n, batch=b, direction="dit", precision="fp32", selection_source="table",
-                         reason="explicit B200 batch local-fused core (selector abstained: " + p.reason + ")",
-                         fallback=False, executed="fft_dit_matrix_batch", block=256,
+                         reason="explicit B200 local-fused core (selector abstained: " + p.reason + ")",
+                         fallback=False, executed=executed, block=256,
                          flow_id="local-fused-tile", flow_realization="matrix-resident",
                          processing_unit="dense-dot-fft64",
                          params={"tile": tile, "rows": 1, "variant": "spread", "batch": b}), "explicit"
+
+
+class Ctx:
+    """Process-group plumbing shared by the workloads."""
+
+    def __init__(self, args):
+        import torch
+        import torch.distributed as dist
+
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != args.gpus and not (self.world == 1 and args.gpus == 1):
+            raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={self.world}")
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            from datetime import timedelta
+
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=self.dev)
+        self.stream = torch.cuda.current_stream(self.dev)
+
+    def barrier(self):
+        if self.world > 1:
+            t = self.torch.ones(1, device=self.dev)
+            self.dist.all_reduce(t)
+        self.torch.cuda.synchronize(self.dev)
+
+    def max_over_ranks(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(self, fn, steps: int):
+        """(max-over-ranks ms of `steps` calls of fn, launches, clocks)."""
+        from bfft import _lib
+
+        torch = self.torch
+        self.barrier()
+        l0 = _lib.launch_counter()
+        with ClockSampler(self.local) as clk:
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record(self.stream)
+            for _ in range(steps):
+                fn()
+            end.record(self.stream)
+            end.synchronize()
+            self.barrier()
+        launches = _lib.launch_counter() - l0
+        return self.max_over_ranks(start.elapsed_time(end)), launches, clk.summary()
+
+    def close(self):
+        if self.world > 1:
+            self.barrier()
+            self.dist.destroy_process_group()
+
+
+def _e2e(ctx, fn_dev, xh, yh, xd, steps):
+    """Public-API call with pinned host in/out, copies inside the timed region."""
+    torch = ctx.torch
+    xd.copy_(xh, non_blocking=True)
+    yh.copy_(fn_dev(xd), non_blocking=True)
+    ctx.barrier()
+    s2 = torch.cuda.Event(enable_timing=True)
+    e2 = torch.cuda.Event(enable_timing=True)
+    s2.record(ctx.stream)
+    for _ in range(steps):
+        xd.copy_(xh, non_blocking=True)
+        yh.copy_(fn_dev(xd), non_blocking=True)
+    e2.record(ctx.stream)
+    e2.synchronize()
+    ctx.barrier()
+    return ctx.max_over_ranks(s2.elapsed_time(e2)) / steps
+
+
+def run_batch(args, wl, ctx) -> dict:
+    """Configs 5a / 3: a batched C2C forward job, rows sharded over ranks."""
+    import bfft
+    from bfft import dist as bdist
+    from bfft.entry import native_plan_for
+
+    torch = ctx.torch
+    n, btot = wl["n"], wl["batch"]
+    first, b = bdist.batch_shard(btot, ctx.world, ctx.rank)
+    plan, plan_src = choose_plan(n, b)
+    g = torch.Generator(device=ctx.dev).manual_seed(SEED + ctx.rank)
+    x = torch.complex(torch.randn(b, n, device=ctx.dev, generator=g), torch.randn(b, n, device=ctx.dev, generator=g))
+    torch.cuda.synchronize(ctx.dev)
+    for _ in range(args.warmup):
+        y = bfft.execute_fft_plan(plan, x)
+    del y
+    native = native_plan_for(plan, ctx.local)
+    elapsed_ms, launches, clocks = ctx.timed(lambda: bfft.execute_fft_plan(plan, x), args.steps)
+    ms_step = elapsed_ms / args.steps
+    value = gflop(n, btot) / (ms_step / 1e3)
+
+    # dominant kernel: every launch of this flow is the CTA-resident pass (or
+    # the cluster kernel); each moves one read + one write of the shard
+    peak, peak_src = measured_peaks()
+    per_launch_ms = ms_step / max(native.launches, 1)
+    bytes_per_launch = 16.0 * n * b
+    achieved = bytes_per_launch / (per_launch_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "k_pass (CTA-resident Stockham pass)", "achieved": achieved,
+                "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
+                "traffic": None, "launches_per_step": native.launches,
+                "algorithmic_bytes_per_launch": bytes_per_launch,
+                "transform_hbm_gbs": 16.0 * n * b / (ms_step / 1e3) / 1e9}
+
+    xh = torch.empty((b, n), dtype=torch.complex64, pin_memory=True)
+    xh.copy_(x)
+    yh = torch.empty((b, n), dtype=torch.complex64, pin_memory=True)
+    xd = torch.empty_like(x)
+    del x
+    e2e_ms = _e2e(ctx, lambda t: bfft.execute_fft_plan(plan, t), xh, yh, xd,
+                  args.e2e_steps or max(1, min(args.steps, 5)))
+    e2e = {"value": gflop(n, btot) / (e2e_ms / 1e3), "unit": "GFLOP/s", "ms_per_step": e2e_ms,
+           "h2d_bytes_per_step": int(xh.numel() * 8) * ctx.world, "d2h_bytes_per_step": int(yh.numel() * 8) * ctx.world,
+           "path": "execute_fft_plan (bfft public API -> libbfft C ABI) with pinned host in/out"}
+    return {"value": value, "ms_step": ms_step, "launches": launches, "clocks": clocks, "roofline": roofline,
+            "e2e": e2e, "scaling": "strong",
+            "config": {"workload": wl["desc"], "n": n, "global_batch": btot, "per_rank_batch": b,
+                       "parallelism": f"batch-shard x{ctx.world} (no data-path collective)",
+                       "l2": "inputs larger than L2 (8 B * N * B per rank >= 512 MiB)",
+                       "plan": plan.executed, "plan_params": plan.params, "plan_source": plan_src},
+            "gflop_per_step": gflop(n, btot)}
+
+
+def run_4step(args, wl, ctx) -> dict:
+    """Config 5b: one transform of N = 2^30.  One GPU: three CTA-resident
+    passes of 2^10; P GPUs: the slab-distributed 4-step with NCCL
+    all-to-alls (bfft.dist.DistributedFFT)."""
+    import bfft
+    from bfft import dist as bdist
+    from bfft.entry import native_plan_for
+
+    torch = ctx.torch
+    n = wl["n"]
+    slab = n // ctx.world
+    g = torch.Generator(device=ctx.dev).manual_seed(SEED + ctx.rank)
+    x = torch.complex(torch.randn(slab, device=ctx.dev, generator=g), torch.randn(slab, device=ctx.dev, generator=g))
+    peak, peak_src = measured_peaks()
+    if ctx.world == 1:
+        plan, plan_src = choose_plan(n, 1)
+        fn = lambda t: bfft.execute_fft_plan(plan, t)  # noqa: E731
+        desc = {"plan": plan.executed, "plan_params": plan.params, "plan_source": plan_src,
+                "parallelism": "1 GPU"}
+    else:
+        f = bdist.DistributedFFT(n, device=ctx.dev)
+        fn = f.execute
+        desc = {"plan": "DistributedFFT (4-step, NCCL all_to_all_single x3)", "factors": [f.n1, f.n2],
+                "parallelism": f"slab x{ctx.world}, 3 all-to-alls per transform"}
+    for _ in range(args.warmup):
+        y = fn(x)
+    del y
+    elapsed_ms, launches, clocks = ctx.timed(lambda: fn(x), args.steps)
+    ms_step = elapsed_ms / args.steps
+    value = gflop(n, 1) / (ms_step / 1e3)
+    if ctx.world == 1:
+        native = native_plan_for(plan, ctx.local)
+        per_launch_ms = ms_step / max(native.launches, 1)
+        bpl = 16.0 * n
+        roofline = {"bound": "hbm", "kernel": "k_pass (CTA-resident Stockham pass)",
+                    "achieved": bpl / (per_launch_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                    "peak_source": peak_src, "traffic": None, "launches_per_step": native.launches,
+                    "algorithmic_bytes_per_launch": bpl, "transform_hbm_gbs": 16.0 * n / (ms_step / 1e3) / 1e9}
+    else:
+        # the exchanges bound this path: 3 all-to-alls, each sending (P-1)/P
+        # of the rank's slab over NVLink
+        wire = 3.0 * 8.0 * slab * (ctx.world - 1) / ctx.world
+        nvl = wire / (ms_step / 1e3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "whole step (transposes, row passes, NCCL all-to-alls)",
+                    "achieved": 16.0 * slab / (ms_step / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                    "peak_source": peak_src, "traffic": None,
+                    "nvlink": {"bytes_per_step_per_gpu": wire, "achieved_gbs_per_direction": nvl,
+                               "peak_gbs_per_direction": 770.0, "frac": nvl / 770.0,
+                               "peak_source": "measured peer copy on this pool (recipe figure)"}}
+    roofline["frac"] = roofline["achieved"] / peak
+
+    xh = torch.empty(slab, dtype=torch.complex64, pin_memory=True)
+    xh.copy_(x)
+    yh = torch.empty(slab, dtype=torch.complex64, pin_memory=True)
+    xd = torch.empty_like(x)
+    del x
+    e2e_ms = _e2e(ctx, fn, xh, yh, xd, args.e2e_steps or 2)
+    e2e = {"value": gflop(n, 1) / (e2e_ms / 1e3), "unit": "GFLOP/s", "ms_per_step": e2e_ms,
+           "h2d_bytes_per_step": 8 * n, "d2h_bytes_per_step": 8 * n,
+           "path": ("execute_fft_plan" if ctx.world == 1 else "DistributedFFT.execute") +
+                   " with pinned host slabs in/out"}
+    return {"value": value, "ms_step": ms_step, "launches": launches, "clocks": clocks, "roofline": roofline,
+            "e2e": e2e, "scaling": "strong",
+            "config": {"workload": wl["desc"], "n": n, "global_batch": 1,
+                       "l2": "input 8 GiB, larger than L2", **desc},
+            "gflop_per_step": gflop(n, 1)}
 
 
 def main() -> None:
@@ -235,131 +443,27 @@ def main() -> None:
         run_reference_arm(args, wl)
         return
 
-    import torch
-    import torch.distributed as dist
-
-    import bfft
-    from bfft import _lib
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus and not (world == 1 and args.gpus == 1):
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-
-    def barrier():
-        if world > 1:
-            t = torch.ones(1, device=dev)
-            dist.all_reduce(t)
-        torch.cuda.synchronize(dev)
-
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    n, btot = wl["n"], wl["batch"]
-    if btot % world:
-        raise SystemExit(f"batch {btot} does not split over {world} ranks")
-    b = btot // world
-    plan, plan_src = choose_plan(n, b)
-    g = torch.Generator(device=dev).manual_seed(SEED + rank)
-    x = torch.complex(torch.randn(b, n, device=dev, generator=g), torch.randn(b, n, device=dev, generator=g))
-    torch.cuda.synchronize(dev)
-
-    # ---- device-timed steps (inputs resident in HBM, 4 GiB > L2) ----
-    for _ in range(args.warmup):
-        y = bfft.execute_fft_plan(plan, x)
-    del y
-    from bfft.entry import native_plan_for
-
-    native = native_plan_for(plan, local)
-    stream = torch.cuda.current_stream(dev)
-    barrier()
-    l0 = _lib.launch_counter()
-    with ClockSampler(local) as clk:
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        for _ in range(args.steps):
-            y = bfft.execute_fft_plan(plan, x)
-        end.record(stream)
-        end.synchronize()
-        barrier()
-    launches = _lib.launch_counter() - l0
-    elapsed_ms = max_over_ranks(start.elapsed_time(end))
-    clocks = clk.summary()
-    del y
-    ms_step = elapsed_ms / args.steps
-    value = gflop(n, btot) / (ms_step / 1e3)
-
-    # ---- dominant kernel roofline: every launch of this flow is the
-    # CTA-resident pass; each moves one read + one write of the shard ----
-    peak, peak_src = measured_peaks()
-    per_launch_ms = ms_step / max(native.launches, 1)
-    bytes_per_launch = 16.0 * n * b
-    achieved = bytes_per_launch / (per_launch_ms / 1e3) / 1e9
-    roofline = {"bound": "hbm", "kernel": "k_pass (CTA-resident Stockham pass)", "achieved": achieved,
-                "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
-                "traffic": None, "launches_per_step": native.launches,
-                "algorithmic_bytes_per_launch": bytes_per_launch,
-                "transform_hbm_gbs": 16.0 * n * b / (ms_step / 1e3) / 1e9}
-
-    # ---- end to end through the public API with pinned host buffers ----
-    e2e_steps = args.e2e_steps or max(1, min(args.steps, 5))
-    xh = torch.empty((b, n), dtype=torch.complex64, pin_memory=True)
-    xh.copy_(x)
-    yh = torch.empty((b, n), dtype=torch.complex64, pin_memory=True)
-    xd = torch.empty_like(x)
-    del x
-    for _ in range(1):
-        xd.copy_(xh, non_blocking=True)
-        yh.copy_(bfft.execute_fft_plan(plan, xd), non_blocking=True)
-    barrier()
-    s2 = torch.cuda.Event(enable_timing=True)
-    e2 = torch.cuda.Event(enable_timing=True)
-    s2.record(stream)
-    for _ in range(e2e_steps):
-        xd.copy_(xh, non_blocking=True)
-        yh.copy_(bfft.execute_fft_plan(plan, xd), non_blocking=True)
-    e2.record(stream)
-    e2.synchronize()
-    barrier()
-    e2e_ms = max_over_ranks(s2.elapsed_time(e2)) / e2e_steps
-    e2e = {"value": gflop(n, btot) / (e2e_ms / 1e3), "unit": "GFLOP/s", "ms_per_step": e2e_ms,
-           "h2d_bytes_per_step": int(xh.numel() * 8), "d2h_bytes_per_step": int(yh.numel() * 8),
-           "path": "execute_fft_plan (bfft public API -> libbfft C ABI) with pinned host in/out"}
+    ctx = Ctx(args)
+    res = run_4step(args, wl, ctx) if wl.get("kind") == "4step" else run_batch(args, wl, ctx)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = reference_cpu(n, 15.0, os.cpu_count() or 1)
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline:
+        cpu_n = wl.get("cpu_n", wl["n"])
+        cpu = reference_cpu(cpu_n, 15.0, 1 if wl.get("kind") == "4step" else (os.cpu_count() or 1))
         cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
-    if rank == 0:
+    if ctx.rank == 0:
         line = {
             "metric": "complex64 C2C FFT GFLOP/s (5N*log2N/t) and HBM GB/s vs roofline",
-            "value": value, "unit": "GFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "complex64", "data": f"synthetic iid N(0,1) re/im, per-rank generator seed {SEED}+rank",
-            "config": {"workload": wl["desc"], "n": n, "global_batch": btot, "per_rank_batch": b,
-                       "parallelism": f"batch-shard x{world} (no data-path collective)",
-                       "l2": "inputs larger than L2 (8 B * N * B per rank >= 512 MiB)",
-                       "plan": plan.executed, "plan_params": plan.params, "plan_source": plan_src},
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
-            "clocks": clocks,
+            "value": res["value"], "unit": "GFLOP/s", "n_gpus": ctx.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["ms_step"], "higher_is_better": True,
+            "scaling": res["scaling"], "vs_baseline": None, "dtype": "complex64",
+            "data": f"synthetic iid N(0,1) re/im, per-rank generator seed {SEED}+rank",
+            "config": res["config"], "roofline": res["roofline"], "cpu_baseline": cpu, "e2e": res["e2e"],
+            "gpu_launches": int(res["launches"]), "clocks": res["clocks"],
         }
         print(json.dumps(line), flush=True)
-    if world > 1:
-        barrier()
-        dist.destroy_process_group()
+    ctx.close()
 
 
 if __name__ == "__main__":

@@ -184,6 +184,43 @@ BFFT_EXPORT bfft_status bfft_hybrid_c2c_noalloc(const void* in, void* out, int64
                                                 int64_t tile, int32_t transform_direction, int32_t norm,
                                                 int32_t device, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Multi-GPU paths.  The reference runs on one device only; these entry points
+ * have no counterpart there and carry its single-device transforms across
+ * ranks.  The host owns the process group and issues the exchanges (NCCL
+ * all-to-all over NVLink); every call below touches this rank's device
+ * memory only.
+ *
+ * Batch sharding (config 5a): rows [first, first + count) of a (batch, n)
+ * job belong to `rank`; the first batch % nranks ranks take one extra row.
+ * Each rank then runs an ordinary plan (bfft_plan_create) on its rows. */
+BFFT_EXPORT bfft_status bfft_dist_batch_shard(int64_t batch, int32_t nranks, int32_t rank, int64_t* first,
+                                              int64_t* count);
+
+/* Distributed 4-step C2C of one transform of N = n1 * n2 points (config 5b),
+ * the reference's hybrid 4-step (src/xpu/adapter_hybrid.py:224-270, N = T*R)
+ * with the transposes that cross ranks done as all-to-alls.  Rank r holds the
+ * contiguous slab x[r N/P, (r+1) N/P) on input and X[r N/P, (r+1) N/P) on
+ * output (natural order), P = nranks (a power of two dividing n1 and n2).
+ * One execution is
+ *     phase 0 -> all-to-all -> phase 1 -> all-to-all -> phase 2 -> all-to-all -> phase 3
+ * where each all-to-all exchanges equal chunks of N/P^2 complex64 (chunk s of
+ * the send buffer goes to rank s; chunk p of the receive buffer comes from
+ * rank p) and phase k+1 reads the receive buffer of the exchange before it.
+ * With nranks = 1 the exchanges are identities (phase k+1 reads phase k's
+ * output).  Every phase writes N/P complex64 to `out`; phases 1 and 2 need
+ * bfft_dist_workspace_size bytes of workspace.  Row FFT tiles 0 = default. */
+typedef struct bfft_dist_plan_s* bfft_dist_plan_t;
+BFFT_EXPORT bfft_status bfft_dist_plan_create(int64_t n1, int64_t n2, int32_t nranks, int32_t rank,
+                                              int32_t transform_direction, int32_t norm, int32_t row_tile1,
+                                              int32_t row_tile2, int32_t device, bfft_dist_plan_t* plan);
+BFFT_EXPORT bfft_status bfft_dist_workspace_size(bfft_dist_plan_t plan, size_t* bytes);
+BFFT_EXPORT bfft_status bfft_dist_phase(bfft_dist_plan_t plan, int32_t phase, const void* in, void* out,
+                                        void* workspace, size_t workspace_bytes, void* stream);
+/* Kernel launches one bfft_dist_phase call of `phase` enqueues. */
+BFFT_EXPORT bfft_status bfft_dist_plan_launches(bfft_dist_plan_t plan, int32_t phase, int* launches);
+BFFT_EXPORT bfft_status bfft_dist_plan_destroy(bfft_dist_plan_t plan);
+
 /* Total kernels this library has enqueued in this process (all devices). */
 BFFT_EXPORT uint64_t bfft_launch_counter(void);
 

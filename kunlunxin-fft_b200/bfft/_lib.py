@@ -29,7 +29,9 @@ VARIANT_IDS = {"spread": 0, "folded": 1}
 EXPORTS = ("bfft_api_version", "bfft_last_error", "bfft_plan_create", "bfft_plan_workspace_size",
            "bfft_plan_launches", "bfft_execute", "bfft_plan_destroy", "bfft_bit_reverse_permute",
            "bfft_r2c_stitch", "bfft_c2r_pre", "bfft_c2r_unpack", "bfft_twiddle_table",
-           "bfft_index_map", "bfft_launch_counter", "bfft_hybrid_c2c_noalloc")
+           "bfft_index_map", "bfft_launch_counter", "bfft_hybrid_c2c_noalloc",
+           "bfft_dist_batch_shard", "bfft_dist_plan_create", "bfft_dist_workspace_size",
+           "bfft_dist_phase", "bfft_dist_plan_launches", "bfft_dist_plan_destroy")
 
 
 class PlanDesc(ctypes.Structure):
@@ -81,6 +83,12 @@ def load() -> ctypes.CDLL:
         L.bfft_twiddle_table.argtypes = [vp, i64, i64, i32, vp]
         L.bfft_index_map.argtypes = [i32, i32, vp, i32, vp]
         L.bfft_hybrid_c2c_noalloc.argtypes = [vp, vp, i64, i64, i64, i32, i32, i32, vp]
+        L.bfft_dist_batch_shard.argtypes = [i64, i32, i32, ctypes.POINTER(i64), ctypes.POINTER(i64)]
+        L.bfft_dist_plan_create.argtypes = [i64, i64, i32, i32, i32, i32, i32, i32, i32, ctypes.POINTER(vp)]
+        L.bfft_dist_workspace_size.argtypes = [vp, ctypes.POINTER(sz)]
+        L.bfft_dist_phase.argtypes = [vp, i32, vp, vp, vp, sz, vp]
+        L.bfft_dist_plan_launches.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_int)]
+        L.bfft_dist_plan_destroy.argtypes = [vp]
         for name in EXPORTS:
             fn = getattr(L, name)
             if name not in ("bfft_api_version", "bfft_last_error", "bfft_launch_counter"):
@@ -138,6 +146,49 @@ class NativePlan:
     def execute(self, in_ptr: int, out_ptr: int, ws_ptr: int, ws_bytes: int, stream: int) -> None:
         check(load().bfft_execute(self.handle, in_ptr, out_ptr, ws_ptr, ws_bytes, stream),
               "bfft_execute")
+
+
+def _destroy_dist(handle: int) -> None:
+    try:
+        if _lib is not None and handle:
+            _lib.bfft_dist_plan_destroy(ctypes.c_void_p(handle))
+    except Exception:  # noqa: BLE001 - interpreter shutdown
+        pass
+
+
+class NativeDistPlan:
+    """Owns one bfft_dist_plan_t (the device phases of the distributed 4-step)."""
+
+    def __init__(self, n1: int, n2: int, nranks: int, rank: int, *, transform_direction: str = "forward",
+                 norm: str = "backward", row_tiles: tuple[int, int] = (0, 0), device: int = 0):
+        L = load()
+        h = ctypes.c_void_p()
+        check(L.bfft_dist_plan_create(int(n1), int(n2), int(nranks), int(rank),
+                                      TRANSFORM_DIRECTION_IDS[transform_direction], NORM_IDS[norm],
+                                      int(row_tiles[0]), int(row_tiles[1]), int(device), ctypes.byref(h)),
+              "bfft_dist_plan_create")
+        self.handle = h.value
+        ws = ctypes.c_size_t()
+        check(L.bfft_dist_workspace_size(self.handle, ctypes.byref(ws)), "bfft_dist_workspace_size")
+        self.workspace_bytes = int(ws.value)
+        self.launches = []
+        for ph in range(4):
+            nl = ctypes.c_int()
+            check(L.bfft_dist_plan_launches(self.handle, ph, ctypes.byref(nl)), "bfft_dist_plan_launches")
+            self.launches.append(int(nl.value))
+        self._fin = weakref.finalize(self, _destroy_dist, self.handle)
+
+    def phase(self, phase: int, in_ptr: int, out_ptr: int, ws_ptr: int, ws_bytes: int, stream: int) -> None:
+        check(load().bfft_dist_phase(self.handle, int(phase), in_ptr, out_ptr, ws_ptr, ws_bytes, stream),
+              "bfft_dist_phase")
+
+
+def batch_shard(batch: int, nranks: int, rank: int) -> tuple[int, int]:
+    """(first row, row count) of `rank` in a batch split over `nranks` (bfft_dist_batch_shard)."""
+    first, count = ctypes.c_int64(), ctypes.c_int64()
+    check(load().bfft_dist_batch_shard(int(batch), int(nranks), int(rank), ctypes.byref(first),
+                                       ctypes.byref(count)), "bfft_dist_batch_shard")
+    return int(first.value), int(count.value)
 
 
 def make_desc(runner: str, direction: str, n: int, batch: int, *, transform_type: str = "c2c",

@@ -1,0 +1,150 @@
+"""Multi-GPU paths: batch sharding and the distributed 4-step transform.
+
+The reference runs on one device; these are its single-device transforms
+carried across the ranks of a ``torch.distributed`` process group, one
+process per GPU (NCCL over NVLink on B200, ``gloo`` for the CPU tests).
+
+* Batch sharding (a batched C2C / R2C / C2R job whose rows are independent):
+  ``batch_shard`` gives each rank a contiguous block of rows
+  (``bfft_dist_batch_shard``) and the rank runs an ordinary plan on them.  No
+  collective touches the data path.
+* ``DistributedFFT``: one 1-D C2C transform of N = N1 * N2 points held as
+  contiguous slabs, computed with the reference's hybrid 4-step
+  decomposition (``src/xpu/adapter_hybrid.py:224-270``) whose three
+  transposes become all-to-alls (``all_to_all_single``, equal chunks) between
+  the four device phases of ``bfft_dist_phase``.
+
+The device phases come from libbfft.so; there is no CPU fallback.  The
+``phases`` argument of ``DistributedFFT`` exists so the orchestration can be
+exercised on CPU ranks with a host restatement of the phases standing in for
+the device (tests only).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+
+def _group_info(group) -> tuple[int, int]:
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_world_size(group), dist.get_rank(group)
+    return 1, 0
+
+
+def batch_shard(batch: int, world: int | None = None, rank: int | None = None, group=None) -> tuple[int, int]:
+    """(first row, row count) of this rank's block of a ``batch``-row job.
+
+    Rows are split contiguously; the first ``batch % world`` ranks take one
+    extra row (the rule of ``bfft_dist_batch_shard``)."""
+    if world is None or rank is None:
+        w, r = _group_info(group)
+        world = w if world is None else world
+        rank = r if rank is None else rank
+    return _lib.batch_shard(batch, world, rank)
+
+
+def default_factors(n: int, world: int = 1) -> tuple[int, int]:
+    """N = N1 * N2 with N1 = 2^ceil(log2 N / 2), N2 = N / N1 (2^15 x 2^15 at
+    N = 2^30)."""
+    if n < 4 or n & (n - 1):
+        raise ValueError(f"n must be a power of two >= 4, got {n}")
+    l = int(math.log2(n))
+    n1 = 1 << ((l + 1) // 2)
+    return n1, n // n1
+
+
+class _NativePhases:
+    """Device phases of one rank (bfft_dist_phase on the current stream)."""
+
+    def __init__(self, n1: int, n2: int, world: int, rank: int, transform_direction: str, norm: str,
+                 device: torch.device, row_tiles: tuple[int, int]):
+        if device.type != "cuda":
+            raise RuntimeError("DistributedFFT needs a CUDA device (there is no CPU fallback)")
+        self.device = device
+        self.plan = _lib.NativeDistPlan(n1, n2, world, rank, transform_direction=transform_direction, norm=norm,
+                                        row_tiles=row_tiles, device=device.index or 0)
+        self.ws = torch.empty(max(self.plan.workspace_bytes, 16), dtype=torch.uint8, device=device)
+        self.launches = sum(self.plan.launches)
+
+    def empty(self, count: int) -> torch.Tensor:
+        return torch.empty(count, dtype=torch.complex64, device=self.device)
+
+    def phase(self, k: int, x: torch.Tensor, out: torch.Tensor) -> None:
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        self.plan.phase(k, x.data_ptr(), out.data_ptr(), self.ws.data_ptr(), self.ws.numel(), stream)
+
+
+class DistributedFFT:
+    """One C2C transform of ``n`` points over the ranks of ``group``.
+
+    Rank r passes its slab ``x[r n/P : (r+1) n/P]`` (complex64, 1-D,
+    contiguous, on its device) and receives ``X[r n/P : (r+1) n/P]`` of the
+    transform in natural order, with the reference's ``transform_direction``
+    and ``norm`` semantics (src/xpu/entry.py:81-102, :619-621).  P must be a
+    power of two dividing both factors of ``n = n1 * n2``."""
+
+    def __init__(self, n: int, *, n1: int | None = None, group=None, transform_direction: str = "forward",
+                 norm: str = "backward", device=None, row_tiles: tuple[int, int] = (0, 0), phases=None):
+        if transform_direction not in ("forward", "inverse"):
+            raise ValueError(f"transform_direction must be 'forward' or 'inverse', got {transform_direction!r}")
+        if norm not in ("none", "forward", "backward", "ortho"):
+            raise ValueError(f"norm must be none/forward/backward/ortho, got {norm!r}")
+        self.world, self.rank = _group_info(group)
+        if n1 is None:
+            n1, n2 = default_factors(n, self.world)
+        else:
+            if n1 < 2 or n1 & (n1 - 1) or n % n1:
+                raise ValueError(f"n1={n1} must be a power of two dividing n={n}")
+            n2 = n // n1
+        if n2 < 2 or n1 % self.world or n2 % self.world:
+            raise ValueError(f"world size {self.world} must divide both factors {n1} x {n2}")
+        self.n, self.n1, self.n2, self.group = n, n1, n2, group
+        self.slab = n // self.world
+        self.transform_direction, self.norm = transform_direction, norm
+        if phases is None:
+            dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+            phases = _NativePhases(n1, n2, self.world, self.rank, transform_direction, norm, dev, row_tiles)
+        self.phases = phases
+        self._bufs = None
+
+    @property
+    def launches(self) -> int:
+        """Device kernels one execute() enqueues on this rank."""
+        return getattr(self.phases, "launches", 0)
+
+    def _buffers(self):
+        if self._bufs is None:
+            self._bufs = (self.phases.empty(self.slab), self.phases.empty(self.slab))
+        return self._bufs
+
+    def _exchange(self, send: torch.Tensor, recv: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return send
+        dist.all_to_all_single(recv, send, group=self.group)
+        return recv
+
+    def execute(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        if not isinstance(x, torch.Tensor):
+            raise TypeError("x must be a torch.Tensor")
+        if x.dtype != torch.complex64:
+            raise TypeError(f"x must be complex64, got {x.dtype}")
+        if x.dim() != 1 or x.numel() != self.slab or not x.is_contiguous():
+            raise ValueError(f"x must be a contiguous 1-D slab of {self.slab} points, got {tuple(x.shape)}")
+        a, b = self._buffers()
+        if out is None:
+            out = self.phases.empty(self.slab)
+        self.phases.phase(0, x, a)
+        cur = self._exchange(a, b)
+        for k in (1, 2):
+            dst = a if cur is b else b
+            self.phases.phase(k, cur, dst)
+            other = b if dst is a else a
+            cur = self._exchange(dst, other)
+        self.phases.phase(3, cur, out)
+        return out
+
+    __call__ = execute
