@@ -562,9 +562,10 @@ struct PassKGeo {
     static constexpr int E = L < 16 ? L : 16;
     static constexpr int TF = L / E;
     static constexpr int LPAD = (L + (L >> 4)) | 1;  // odd: regions start on distinct banks
-    // sub-FFTs per CTA: ~256 threads; >= 4 when the sub-FFT index is the
-    // coalesced dimension; capped so two tile buffers fit in 200 KB.
-    static constexpr int KMIN = (LAYOUT || SMAP == 2) ? 4 : 1;
+    // sub-FFTs per CTA: ~256 threads; >= 16 when the sub-FFT index is the
+    // coalesced dimension (128-byte runs per element index: shorter runs
+    // leave HBM bursts half used); capped so two tile buffers fit in 200 KB.
+    static constexpr int KMIN = (LAYOUT || SMAP == 2) ? 16 : 1;
     static constexpr int K0 = TF >= 256 ? 1 : 256 / TF;
     static constexpr int KD = K0 > KMIN ? K0 : KMIN;
     static constexpr int KCAP = floor_pow2((200 * 1024) / (2 * LPAD * 8));
@@ -586,6 +587,26 @@ __global__ void __launch_bounds__(PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>::THREADS,
     int64_t* sbase = reinterpret_cast<int64_t*>(smem + 2 * G::K * G::LPAD);
     float2* tw_smem = reinterpret_cast<float2*>(sbase + G::K);
     fill_stockham_twiddles<LOG2L>(tw_smem);  // visible after the first in-loop barrier
+    // The plan's two-level W_N tables, copied to shared memory when they fit
+    // (launch_pass decides): pre/post twiddles then cost two shared loads.
+    float2* tw2 = tw_smem + tw_total(LOG2L);
+    const bool tws = a.tw_smem_entries > 0;
+    const int lo_bits = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
+    const uint32_t lo_mask = (1u << lo_bits) - 1u;
+    if (tws) {
+        const int nlo = 1 << lo_bits, nhi = a.tw.log2n > lo_bits ? 1 << (a.tw.log2n - lo_bits) : 0;
+        for (int i = threadIdx.x; i < nlo; i += blockDim.x) tw2[i] = a.tw.lo[i];
+        for (int i = threadIdx.x; i < nhi; i += blockDim.x) tw2[nlo + i] = a.tw.hi[i];
+        __syncthreads();
+    }
+    const float2* tw2hi = tw2 + (1 << lo_bits);
+    const uint32_t nmask = a.tw.log2n >= 32 ? 0xffffffffu : (1u << a.tw.log2n) - 1u;
+    auto twiddle = [&](uint32_t e) -> float2 {
+        if (!tws) return tw_two_level(a.tw, e);
+        e &= nmask;
+        const float2 w = tw2[e & lo_mask];
+        return a.tw.log2n > lo_bits ? cmul(w, tw2hi[e >> lo_bits]) : w;
+    };
     const int tid = threadIdx.x;
     const int cl = LAYOUT ? tid % G::K : tid / G::TF;
     const int t = LAYOUT ? tid / G::K : tid % G::TF;
@@ -646,7 +667,7 @@ __global__ void __launch_bounds__(PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>::THREADS,
             const int e = t + m * G::TF;
             float2 val = region[pad16(e)];
             if (a.conj_in) val.y = -val.y;
-            if (a.tw_mode == 1) val = cmul(val, tw_two_level(a.tw, (uint32_t)e * cmul32));
+            if (a.tw_mode == 1) val = cmul(val, twiddle((uint32_t)e * cmul32));
             v[m] = val;
         }
         if (G::NP > 1 || SMAP != 0) __syncthreads();  // buffer becomes the exchange area
@@ -657,7 +678,7 @@ __global__ void __launch_bounds__(PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>::THREADS,
         for (int m = 0; m < G::E; ++m) {
             const int k = t + m * G::TF;
             float2 val = v[m];
-            if (a.tw_mode == 2) val = cmul(val, tw_two_level(a.tw, (uint32_t)k * cmul32));
+            if (a.tw_mode == 2) val = cmul(val, twiddle((uint32_t)k * cmul32));
             v[m] = make_float2(val.x * osr, val.y * osi);
         }
 
@@ -698,30 +719,49 @@ template <int LOG2L, int LAYOUT, int LMAP, int SMAP>
 static cudaError_t launch_pass_t(const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
     using G = PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>;
     auto kern = k_pass<LOG2L, LAYOUT, LMAP, SMAP>;
-    static int blocks_per_sm[64] = {0};
+    // Shared-memory W_N tables: up to kTw2Max entries (N <= 2^22), size
+    // class c holds 2^c entries; occupancy is cached per device and class.
+    constexpr int kTw2MaxLog2 = 12;
+    constexpr size_t kSmemCap = 227 * 1024;
+    static int blocks_per_sm[64][kTw2MaxLog2 + 2] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (blocks_per_sm[dev] == 0) {
-        if (G::SMEM > 48 * 1024) {
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::SMEM);
+    PassArgs b = a;
+    b.tw_smem_entries = 0;
+    int cls = 0;
+    if (a.tw_mode != 0) {
+        const int lob = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
+        const int nlo = 1 << lob, nhi = a.tw.log2n > lob ? 1 << (a.tw.log2n - lob) : 0;
+        int c = 0;
+        while ((1 << c) < nlo + nhi) ++c;
+        if (c <= kTw2MaxLog2 && G::SMEM + ((size_t)sizeof(float2) << c) <= kSmemCap) {
+            b.tw_smem_entries = nlo + nhi;
+            cls = c + 1;
+        }
+    }
+    const size_t smem_cls = G::SMEM + (cls ? ((size_t)sizeof(float2) << (cls - 1)) : 0);
+    if (blocks_per_sm[dev][cls] == 0) {
+        if (smem_cls > 48 * 1024) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
             if (e != cudaSuccess) return e;
         }
         int nb = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, G::THREADS, G::SMEM);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, G::THREADS, smem_cls);
         if (e != cudaSuccess) return e;
         if (g_num_sms == 0) {
             e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
             if (e != cudaSuccess) return e;
         }
-        blocks_per_sm[dev] = nb > 0 ? nb : 1;
+        blocks_per_sm[dev][cls] = nb > 0 ? nb : 1;
     }
-    const int64_t ntiles = (a.nsub + G::K - 1) / G::K;
-    int64_t grid = (int64_t)blocks_per_sm[dev] * g_num_sms;
+    const int64_t ntiles = (b.nsub + G::K - 1) / G::K;
+    int64_t grid = (int64_t)blocks_per_sm[dev][cls] * g_num_sms;
     if (grid > ntiles) grid = ntiles;
     if (grid < 1) grid = 1;
-    kern<<<(unsigned)grid, G::THREADS, G::SMEM, s>>>(in, out, a);
+    const size_t smem = G::SMEM + (size_t)b.tw_smem_entries * sizeof(float2);
+    kern<<<(unsigned)grid, G::THREADS, smem, s>>>(in, out, b);
     return cudaGetLastError();
 }
 

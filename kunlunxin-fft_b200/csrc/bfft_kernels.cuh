@@ -101,6 +101,7 @@ struct PassArgs {
     float scale;
     int conj_in, conj_out;
     const float2* unit_tw;  // unit twiddle levels (ensure_unit_twiddles)
+    int tw_smem_entries;    // set by launch_pass: > 0 = the W_N tables are copied to shared memory
 };
 
 constexpr int kMaxPassLog2 = 12;  // largest CTA-resident sub-FFT: 4096 points
