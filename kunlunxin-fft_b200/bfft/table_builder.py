@@ -446,6 +446,29 @@ def build_table(runs: list[dict], *, guard_pct: float = GUARD_PCT, sources: list
     return table
 
 
+# ---------------------------------------------------------------- run files
+
+def save_run(run: dict, path: str) -> None:
+    """Write a run file (gzip-compressed when ``path`` ends in .gz)."""
+    import gzip
+
+    blob = json.dumps(run, separators=(",", ":")).encode()
+    if path.endswith(".gz"):
+        with gzip.open(path, "wb", compresslevel=9) as f:
+            f.write(blob)
+    else:
+        with open(path, "wb") as f:
+            f.write(blob)
+
+
+def load_run(path: str) -> dict:
+    import gzip
+
+    opener = gzip.open if path.endswith(".gz") else open
+    with opener(path, "rb") as f:
+        return json.loads(f.read().decode())
+
+
 # ---------------------------------------------------------------- CLI
 
 def main(argv=None) -> int:
@@ -466,13 +489,9 @@ def main(argv=None) -> int:
     if a.cmd == "measure":
         run = measure(default_shapes(a.quick), sessions=a.sessions, trials=a.trials, warmup=a.warmup,
                       device=a.device, log=lambda s: print(s, file=sys.stderr, flush=True))
-        with open(a.out, "w") as f:
-            json.dump(run, f, indent=1)
+        save_run(run, a.out)
         return 0
-    runs = []
-    for p in a.runs:
-        with open(p) as f:
-            runs.append(json.load(f))
+    runs = [load_run(p) for p in a.runs]
     table = build_table(runs, guard_pct=a.guard_pct, sources=[os.path.basename(p) for p in a.runs])
     with open(a.out, "w") as f:
         json.dump(table, f, indent=1)

@@ -364,3 +364,36 @@ def test_cluster_single_pass(log2n):
     from bfft.entry import native_plan_for
 
     assert native_plan_for(_plan("fft_dit_matrix_batch", n, 64, params={"tile": n}), 0).launches == 1
+
+
+def test_installed_b200_table_selects_and_executes():
+    """The committed B200 selector table binds this environment: plan_fft with
+    the live profile selects measured entries (legacy and semantic tiers) and
+    they execute within tolerance."""
+    from bfft.config import DeviceProfile
+    from bfft.envcheck import current_env_hash
+    from bfft.selector import load_table
+
+    table = load_table()
+    if current_env_hash() != table["env_hash"]:
+        pytest.skip(f"selector table bound to env {table['env_hash']}, this box is {current_env_hash()}: "
+                    "re-measure with python -m bfft.table_builder")
+    ph = DeviceProfile.load().hash()
+    rng = np.random.default_rng(8)
+    for n, b, tt, td in [(2048, 1, "c2c", "forward"), (1024, 16, "c2c", "inverse"), (65536, 8192 // 64, "c2c", "forward"),
+                         (4096, 256, "r2c", "forward"), (16384, 256, "c2r", "inverse")]:
+        p = bfft.plan_fft("dit", n, batch=b, profile_hash=ph, transform_type=tt, transform_direction=td)
+        if (n, b) != (65536, 128):
+            assert not p.fallback and p.selection_source == "table", (n, b, tt, p.reason)
+        if tt == "r2c":
+            x = rng.standard_normal((b, n)).astype(np.float32)
+            ref = np.fft.rfft(x.astype(np.float64))
+        elif tt == "c2r":
+            x = np.fft.rfft(rng.standard_normal((b, n))).astype(np.complex64)
+            ref = np.fft.irfft(x.astype(np.complex128), n=n)
+        else:
+            x = cplx(rng, (b, n))
+            ref = np.fft.fft(x.astype(np.complex128)) if td == "forward" else np.fft.ifft(x.astype(np.complex128))
+        t = dev(x if b > 1 else x[0])
+        y = host(execute_fft_plan(p, t)).reshape(ref.shape)
+        assert rel_l2_per_transform(y, ref) <= TOL_F64, (n, b, tt, p.executed)
