@@ -73,18 +73,36 @@ class ClockSampler:
         self.proc = None
         self.file = None
 
+    def _lines(self) -> int:
+        try:
+            with open(self.file.name) as f:
+                return sum(1 for r in f if r.strip())
+        except OSError:
+            return 0
+
+    def _wait_lines(self, n: int, limit_s: float) -> None:
+        t0 = time.monotonic()
+        while self._lines() < n and time.monotonic() - t0 < limit_s and self.proc.poll() is None:
+            time.sleep(0.005)
+
     def __enter__(self):
+        # The sampler is running (first sample written) before the timed
+        # region starts; only samples after that point are summarised.
+        self.skip = 0
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "20", "-i", str(self.gpu)], stdout=self.file,
                                          stderr=subprocess.DEVNULL)
+            self._wait_lines(1, 10.0)
+            self.skip = self._lines()
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            self._wait_lines(self.skip + 2, 2.0)  # at least one sample at or after the region's end
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -99,6 +117,7 @@ class ClockSampler:
         with open(self.file.name) as f:
             rows = [r.strip().split(", ") for r in f if r.strip()]
         os.unlink(self.file.name)
+        rows = rows[max(self.skip - 1, 0):]  # the last sample before the region onwards
         sm, mx, reasons = [], [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for r in rows:
