@@ -221,6 +221,12 @@ BFFT_EXPORT bfft_status bfft_dist_phase(bfft_dist_plan_t plan, int32_t phase, co
 BFFT_EXPORT bfft_status bfft_dist_plan_launches(bfft_dist_plan_t plan, int32_t phase, int* launches);
 BFFT_EXPORT bfft_status bfft_dist_plan_destroy(bfft_dist_plan_t plan);
 
+/* Status bits the kernels set on `device` when a bounded wait expired
+ * (bit 0: a TMA pass gave up waiting for a tile copy and returned early, so
+ * its output is incomplete).  Synchronises the device; clear != 0 resets the
+ * word.  Always 0 in a healthy run -- the tests check it. */
+BFFT_EXPORT bfft_status bfft_device_status(int32_t device, uint32_t* status, int32_t clear);
+
 /* Total kernels this library has enqueued in this process (all devices). */
 BFFT_EXPORT uint64_t bfft_launch_counter(void);
 

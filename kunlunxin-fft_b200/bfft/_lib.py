@@ -31,7 +31,7 @@ EXPORTS = ("bfft_api_version", "bfft_last_error", "bfft_plan_create", "bfft_plan
            "bfft_r2c_stitch", "bfft_c2r_pre", "bfft_c2r_unpack", "bfft_twiddle_table",
            "bfft_index_map", "bfft_launch_counter", "bfft_hybrid_c2c_noalloc",
            "bfft_dist_batch_shard", "bfft_dist_plan_create", "bfft_dist_workspace_size",
-           "bfft_dist_phase", "bfft_dist_plan_launches", "bfft_dist_plan_destroy")
+           "bfft_dist_phase", "bfft_dist_plan_launches", "bfft_dist_plan_destroy", "bfft_device_status")
 
 
 class PlanDesc(ctypes.Structure):
@@ -89,6 +89,7 @@ def load() -> ctypes.CDLL:
         L.bfft_dist_phase.argtypes = [vp, i32, vp, vp, vp, sz, vp]
         L.bfft_dist_plan_launches.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_int)]
         L.bfft_dist_plan_destroy.argtypes = [vp]
+        L.bfft_device_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint32), i32]
         for name in EXPORTS:
             fn = getattr(L, name)
             if name not in ("bfft_api_version", "bfft_last_error", "bfft_launch_counter"):
@@ -112,6 +113,13 @@ def check(status: int, what: str = "bfft") -> None:
     if status == ERR_ALLOC:
         raise MemoryError(msg)
     raise RuntimeError(msg)
+
+
+def device_status(device: int = 0, clear: bool = False) -> int:
+    """Status bits the kernels set when a bounded wait expired (0 = healthy)."""
+    v = ctypes.c_uint32()
+    check(load().bfft_device_status(int(device), ctypes.byref(v), 1 if clear else 0), "bfft_device_status")
+    return int(v.value)
 
 
 def launch_counter() -> int:

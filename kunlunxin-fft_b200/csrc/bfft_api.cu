@@ -837,6 +837,17 @@ bfft_status bfft_index_map(int32_t kind, int32_t bits, void* out, int32_t device
     return e == cudaSuccess ? BFFT_OK : cuda_fail(e, "index_map");
 }
 
+bfft_status bfft_device_status(int32_t device, uint32_t* status, int32_t clear) {
+    if (!status) return fail(BFFT_ERR_VALUE, "null pointer");
+    DeviceGuard g(device);
+    if (!g.ok) return fail(BFFT_ERR_CUDA, "cannot select device %d", device);
+    unsigned v = 0;
+    cudaError_t e = read_device_status(&v, clear != 0);
+    if (e != cudaSuccess) return cuda_fail(e, "device_status");
+    *status = v;
+    return BFFT_OK;
+}
+
 bfft_status bfft_twiddle_table(void* w, int64_t n, int64_t count, int32_t device, void* stream) {
     if (!w) return fail(BFFT_ERR_VALUE, "null pointer");
     if (!is_pow2(n)) return fail(BFFT_ERR_SHAPE, "size must be a positive power of two, got %lld", (long long)n);

@@ -487,7 +487,17 @@ __device__ __forceinline__ void fill_stockham_twiddles(float2* tw_smem) {
     }
 }
 
-template <int LOG2L, int PASS, int E, int TF>
+// Exchange addressing: XS = 0 is a padded per-sub-FFT region (element i at
+// pad16(i)); XS > 0 is a dense tile with the sub-FFT index fastest (element i
+// of this sub-FFT at i * XS), conflict-free when 16 or more sub-FFTs share a
+// warp's half.
+template <int XS>
+__device__ __forceinline__ int xaddr(int i) {
+    if constexpr (XS == 0) return pad16(i);
+    else return i * XS;
+}
+
+template <int LOG2L, int PASS, int E, int TF, int XS = 0>
 __device__ __forceinline__ void stockham_passes(float2 (&v)[E], int t, float2* region, const float2* tw_smem) {
     constexpr int NP = LOG2L <= 4 ? 1 : (LOG2L + 3) / 4;
     if constexpr (PASS < NP) {
@@ -518,13 +528,13 @@ __device__ __forceinline__ void stockham_passes(float2 (&v)[E], int t, float2* r
                 const int k = b & ((1 << LP) - 1);
                 const int base = ((b >> LP) << (LP + LR)) + k;
 #pragma unroll
-                for (int j = 0; j < R; ++j) region[pad16(base + (j << LP))] = v[q + j * NB];
+                for (int j = 0; j < R; ++j) region[xaddr<XS>(base + (j << LP))] = v[q + j * NB];
             }
             __syncthreads();
 #pragma unroll
-            for (int m = 0; m < E; ++m) v[m] = region[pad16(t + m * TF)];
+            for (int m = 0; m < E; ++m) v[m] = region[xaddr<XS>(t + m * TF)];
             __syncthreads();
-            stockham_passes<LOG2L, PASS + 1, E, TF>(v, t, region, tw_smem);
+            stockham_passes<LOG2L, PASS + 1, E, TF, XS>(v, t, region, tw_smem);
         }
     }
 }
@@ -781,8 +791,27 @@ static cudaError_t launch_pass_l(int layout, int lmap, int smap, const float2* i
                      : launch_pass_t<LOG2L, 0, 0, 0>(in, out, a, s);
 }
 
+}  // namespace bfft
+
+#include "bfft_pass_tma.cuh"
+
+namespace bfft {
+
+cudaError_t read_device_status(unsigned* status, bool clear) {
+    cudaError_t e = cudaMemcpyFromSymbol(status, g_kernel_status, sizeof(unsigned));
+    if (e == cudaSuccess && clear) {
+        const unsigned zero = 0;
+        e = cudaMemcpyToSymbol(g_kernel_status, &zero, sizeof(unsigned));
+    }
+    return e;
+}
+
 cudaError_t launch_pass(int log2l, int layout, int lmap, int smap, const float2* in, float2* out,
                         const PassArgs& a, cudaStream_t s) {
+    if (layout == 1) {  // column tiles: TMA-staged pass when the shape allows it
+        const cudaError_t e = launch_pass_tma(log2l, in, out, a, s);
+        if (e != cudaErrorNotSupported) return e;
+    }
     switch (log2l) {
         case 1: return launch_pass_l<1>(layout, lmap, smap, in, out, a, s);
         case 2: return launch_pass_l<2>(layout, lmap, smap, in, out, a, s);

@@ -63,6 +63,10 @@ struct ClusterArgs {
 bool cluster_supported(int log2n);
 cudaError_t launch_cluster_fft(int log2n, const float2* in, float2* out, const ClusterArgs& a, cudaStream_t s);
 
+// Status word the kernels set when a bounded wait expires (bit 0: an
+// mbarrier wait of the TMA pass); read synchronously, optionally cleared.
+cudaError_t read_device_status(unsigned* status, bool clear);
+
 // Library-wide error message (bfft_last_error) and launch counter.
 void set_last_error(const char* msg);
 void count_launches(int k);

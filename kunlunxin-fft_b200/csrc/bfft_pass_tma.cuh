@@ -1,0 +1,374 @@
+// bfft_pass_tma.cuh -- the Stockham pass with TMA-staged column tiles.
+//
+// Included by bfft_kernels.cu (one translation unit: it shares the unit
+// twiddle levels and the Stockham helpers).  Same transform as k_pass for the
+// pass shapes whose sub-FFT index is the contiguous dimension of the input
+// (every tail pass of a multi-pass flow, the strided local group, the 4-step
+// column pass): a tile of K sub-FFTs x L elements is one 3-D box of a tensor
+// map [outer][element][sub-FFT], copied by the Tensor Memory Accelerator into
+// a dense [element][sub-FFT] shared-memory tile.  With K >= 16 that layout is
+// bank-conflict free for the column thread mapping (sub-FFT index fastest)
+// without padding, so the same tile is the landing buffer, the Stockham
+// exchange area and the staging buffer of the store -- a TMA tensor store for
+// column outputs, one bulk copy per sub-FFT for row outputs.  No thread
+// computes a global address per element; the copies are asynchronous and
+// tracked by mbarriers (loads) and bulk groups (stores).
+//
+// Pipeline: three stages per CTA, persistent over tiles.  While tile i is
+// transformed in stage i % 3, the load of tile i+1 is in flight into stage
+// (i+1) % 3, whose previous contents (tile i-2) the store engine has finished
+// reading.  No multicast: each CTA loads only its own tiles.
+//
+// Every wait on an mbarrier is bounded (kWaitLimitNs of %globaltimer); on
+// expiry the kernel records a status bit (bfft_device_status), waits once
+// more (bounded) for its copy in flight and returns.
+#pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+namespace bfft {
+
+__device__ unsigned int g_kernel_status;  // bit 0: a bounded mbarrier wait expired
+
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        " .reg .pred p;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for phase `parity` of `b` to complete; false (and status bit 0) when
+// it has not completed within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* b, uint32_t parity) {
+    if (mbar_try_wait(b, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(b, parity)) return true;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(&g_kernel_status, 1u);
+            return false;
+        }
+    }
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int c0, int c1, int c2, const void* src) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+                 "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// Generic-proxy writes to shared memory become visible to the async proxy
+// (the TMA store engine) after this fence and a barrier.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ROWS 0: outputs are columns too (one tensor store per tile);
+// ROWS 1: each sub-FFT's output is a contiguous row (one bulk copy each).
+template <int LOG2L, int ROWS>
+struct PassTGeo {
+    static constexpr int L = 1 << LOG2L;
+    static constexpr int E = 16;
+    static constexpr int TF = L / E;
+    static constexpr int K = (256 / TF) > 16 ? 256 / TF : 16;
+    static constexpr int THREADS = K * TF;
+    static constexpr int LB = L < 256 ? L : 256;  // TMA box extent along the element index
+    static constexpr int RPAD = ROWS ? 2 : 0;     // row staging: 16-byte aligned rows, 2-way conflicts at most
+    static constexpr int SB = ((K * (L + RPAD) * 8) + 1023) / 1024 * 1024;
+    static constexpr int STAGES = 3;
+    static constexpr int MINB = THREADS >= 512 ? 1 : 2;
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * SB + 64 + (size_t)tw_total(LOG2L) * sizeof(float2);
+    static_assert(L >= 16 && K <= 256 && LB <= 256, "TMA box limits");
+};
+
+template <int LOG2L, int ROWS>
+__global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L, ROWS>::MINB)
+    k_pass_tma(const __grid_constant__ CUtensorMap tin, const __grid_constant__ CUtensorMap tout,
+               float2* __restrict__ out, PassArgs a) {
+    using G = PassTGeo<LOG2L, ROWS>;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* base =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + G::STAGES * G::SB);
+    float2* tw_smem = reinterpret_cast<float2*>(full + 8);
+    float2* tw2 = tw_smem + tw_total(LOG2L);
+    auto stage = [&](int s) { return reinterpret_cast<float2*>(base + s * G::SB); };
+
+    const int tid = threadIdx.x;
+    const int cl = tid % G::K, t = tid / G::K;
+    constexpr int NST = ROWS ? G::K : 1;  // threads that issue (and wait for) stores
+    const int64_t ntiles = a.nsub / G::K;
+    const int64_t imask = (int64_t(1) << a.inner_log2) - 1;
+    const float osr = a.scale, osi = a.conj_out ? -a.scale : a.scale;
+
+    fill_stockham_twiddles<LOG2L>(tw_smem);
+    const bool tws = a.tw_smem_entries > 0;
+    const int lo_bits = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
+    const uint32_t lo_mask = (1u << lo_bits) - 1u;
+    if (tws) {
+        const int nlo = 1 << lo_bits, nhi = a.tw.log2n > lo_bits ? 1 << (a.tw.log2n - lo_bits) : 0;
+        for (int i = tid; i < nlo; i += blockDim.x) tw2[i] = a.tw.lo[i];
+        for (int i = tid; i < nhi; i += blockDim.x) tw2[nlo + i] = a.tw.hi[i];
+    }
+    const float2* tw2hi = tw2 + (1 << lo_bits);
+    const uint32_t nmask = a.tw.log2n >= 32 ? 0xffffffffu : (1u << a.tw.log2n) - 1u;
+    auto twiddle = [&](uint32_t e) -> float2 {
+        if (!tws) return tw_two_level(a.tw, e);
+        e &= nmask;
+        const float2 w = tw2[e & lo_mask];
+        return a.tw.log2n > lo_bits ? cmul(w, tw2hi[e >> lo_bits]) : w;
+    };
+    if (tid == 0) {
+        for (int s = 0; s < G::STAGES; ++s) mbar_init(&full[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_proxy_async_smem();
+    }
+    __syncthreads();
+
+    auto issue = [&](int64_t tl, int s) {  // thread 0 only
+        const int64_t f0 = tl * G::K;
+        const int o = static_cast<int>(f0 >> a.inner_log2), c0 = static_cast<int>(f0 & imask);
+        float2* dst = stage(s);
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(G::K * G::L * sizeof(float2)));
+#pragma unroll
+        for (int j = 0; j < G::L / G::LB; ++j) tma_load_3d(dst + j * G::LB * G::K, &tin, c0, j * G::LB, o, &full[s]);
+    };
+
+    int64_t tile = blockIdx.x;
+    if (tid == 0 && tile < ntiles) issue(tile, 0);
+    int it = 0;
+    bool aborted = false;
+    for (; tile < ntiles; ++it, tile += gridDim.x) {
+        const int s = it % G::STAGES;
+        float2* buf = stage(s);
+        const int64_t f = tile * G::K + cl;
+        const int64_t o = f >> a.inner_log2, c = f & imask;
+        // the stores that read the stage the next load will fill (tile it-2) are done reading
+        if (tid < NST) bulk_wait_read<1>();
+        const bool ok = mbar_wait_bounded(&full[s], static_cast<uint32_t>((it / G::STAGES) & 1));
+
+        const uint32_t cmul32 = static_cast<uint32_t>(c) * static_cast<uint32_t>(a.tw_mul);
+        float2 v[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            const uint32_t e = static_cast<uint32_t>(t + m * G::TF);
+            const uint32_t pe = a.in_elem_bitrev ? brev_bits(e, LOG2L) : e;
+            float2 val = ok ? buf[pe * G::K + cl] : make_float2(0.f, 0.f);
+            if (a.conj_in) val.y = -val.y;
+            if (a.tw_mode == 1) val = cmul(val, twiddle(e * cmul32));
+            v[m] = val;
+        }
+        if (__syncthreads_or(!ok)) {  // the tile is now the exchange area
+            aborted = true;
+            break;
+        }
+        if (tid == 0 && tile + gridDim.x < ntiles) issue(tile + gridDim.x, (it + 1) % G::STAGES);
+
+        stockham_passes<LOG2L, 0, 16, G::TF, G::K>(v, t, buf + cl, tw_smem);
+
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            const uint32_t k = static_cast<uint32_t>(t + m * G::TF);
+            float2 val = v[m];
+            if (a.tw_mode == 2) val = cmul(val, twiddle(k * cmul32));
+            val = make_float2(val.x * osr, val.y * osi);
+            if constexpr (ROWS) {
+                buf[cl * (G::L + G::RPAD) + k] = val;
+            } else {
+                const uint32_t pk = a.out_elem_bitrev ? brev_bits(k, LOG2L) : k;
+                buf[pk * G::K + cl] = val;
+            }
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if constexpr (ROWS) {
+            if (tid < G::K) {  // t == 0: this thread's sub-FFT is f
+                const int64_t cout = a.out_base_bits ? static_cast<int64_t>(brev_bits(static_cast<uint32_t>(c), a.out_base_bits)) : c;
+                bulk_store(out + o * a.out_outer + cout * a.out_inner, buf + tid * (G::L + G::RPAD),
+                           static_cast<uint32_t>(G::L * sizeof(float2)));
+                bulk_commit();
+            }
+        } else {
+            if (tid == 0) {
+                const int64_t f0 = tile * G::K;
+                const int oo = static_cast<int>(f0 >> a.inner_log2), c0 = static_cast<int>(f0 & imask);
+#pragma unroll
+                for (int j = 0; j < G::L / G::LB; ++j) tma_store_3d(&tout, c0, j * G::LB, oo, buf + j * G::LB * G::K);
+                bulk_commit();
+            }
+        }
+    }
+    if (aborted && tid == 0)  // the copy this tile waited for may still land: wait (bounded) before leaving
+        mbar_wait_bounded(&full[it % G::STAGES], static_cast<uint32_t>((it / G::STAGES) & 1));
+    if (tid < NST) bulk_wait<0>();
+}
+
+// ---- host side ----
+
+using EncodeTiledFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+static EncodeTiledFn tensor_map_encoder() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 3-D map of complex64 (8-byte elements) [d2][d1][d0] with byte strides s1, s2.
+static bool encode_map_3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                          uint64_t s2, uint32_t b0, uint32_t b1) {
+    EncodeTiledFn enc = tensor_map_encoder();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {s1, s2};
+    cuuint32_t box[3] = {b0, b1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int LOG2L, int ROWS>
+static cudaError_t launch_pass_tma_t(const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
+    using G = PassTGeo<LOG2L, ROWS>;
+    auto kern = k_pass_tma<LOG2L, ROWS>;
+    constexpr int kTw2MaxLog2 = 12;
+    constexpr size_t kSmemCap = 227 * 1024;
+    static int blocks_per_sm[64][kTw2MaxLog2 + 2] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    const uint64_t inner = 1ull << a.inner_log2, nouter = static_cast<uint64_t>(a.nsub) >> a.inner_log2;
+    CUtensorMap tin, tout;
+    if (!encode_map_3d(&tin, in, inner, G::L, nouter, static_cast<uint64_t>(a.in_stride) * 8,
+                       static_cast<uint64_t>(a.in_outer) * 8, G::K, G::LB))
+        return cudaErrorNotSupported;
+    if (ROWS) {
+        tout = tin;  // unused: row outputs are bulk copies
+    } else if (!encode_map_3d(&tout, out, inner, G::L, nouter, static_cast<uint64_t>(a.out_stride) * 8,
+                              static_cast<uint64_t>(a.out_outer) * 8, G::K, G::LB)) {
+        return cudaErrorNotSupported;
+    }
+    PassArgs b = a;
+    b.tw_smem_entries = 0;
+    int cls = 0;
+    if (a.tw_mode != 0) {
+        const int lob = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
+        const int nlo = 1 << lob, nhi = a.tw.log2n > lob ? 1 << (a.tw.log2n - lob) : 0;
+        int c = 0;
+        while ((1 << c) < nlo + nhi) ++c;
+        if (c <= kTw2MaxLog2 && G::SMEM + ((size_t)sizeof(float2) << c) <= kSmemCap) {
+            b.tw_smem_entries = nlo + nhi;
+            cls = c + 1;
+        }
+    }
+    const size_t smem_cls = G::SMEM + (cls ? ((size_t)sizeof(float2) << (cls - 1)) : 0);
+    if (blocks_per_sm[dev][cls] == 0) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
+        if (e != cudaSuccess) return e;
+        int nb = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, G::THREADS, smem_cls);
+        if (e != cudaSuccess) return e;
+        if (g_num_sms == 0) {
+            e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess) return e;
+        }
+        blocks_per_sm[dev][cls] = nb > 0 ? nb : 1;
+    }
+    const int64_t ntiles = b.nsub / G::K;
+    int64_t grid = (int64_t)blocks_per_sm[dev][cls] * g_num_sms;
+    if (grid > ntiles) grid = ntiles;
+    if (grid < 1) grid = 1;
+    const size_t smem = G::SMEM + (size_t)b.tw_smem_entries * sizeof(float2);
+    kern<<<(unsigned)grid, G::THREADS, smem, s>>>(tin, tout, out, b);
+    return cudaGetLastError();
+}
+
+// The TMA pass when the shapes allow it; cudaErrorNotSupported otherwise
+// (the caller then runs k_pass).
+static cudaError_t launch_pass_tma(int log2l, const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
+    if (log2l < 4 || log2l > 9) return cudaErrorNotSupported;
+    const int tf = (1 << log2l) / 16;
+    const int k = (256 / tf) > 16 ? 256 / tf : 16;
+    int lk = 0;
+    while ((1 << lk) < k) ++lk;
+    const bool aligned = ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+    if (!aligned || a.inner_log2 < lk || a.inner_log2 > 30 || (a.nsub & ((int64_t(1) << a.inner_log2) - 1)) ||
+        (a.nsub >> a.inner_log2) >= (int64_t(1) << 31))
+        return cudaErrorNotSupported;
+    if (a.in_inner != 1 || a.in_base_bits || (a.in_stride & 1) || (a.in_outer & 1) || a.in_stride <= 0)
+        return cudaErrorNotSupported;
+    const bool col_out = a.out_inner == 1 && !a.out_base_bits && !(a.out_stride & 1) && !(a.out_outer & 1) &&
+                         a.out_stride > 0;
+    const bool row_out = a.out_stride == 1 && !a.out_elem_bitrev && !(a.out_inner & 1) && !(a.out_outer & 1);
+    if (!col_out && !row_out) return cudaErrorNotSupported;
+#define BFFT_TMA_CASE(L)                                                                             \
+    case L:                                                                                          \
+        return col_out ? launch_pass_tma_t<L, 0>(in, out, a, s) : launch_pass_tma_t<L, 1>(in, out, a, s);
+    switch (log2l) {
+        BFFT_TMA_CASE(4)
+        BFFT_TMA_CASE(5)
+        BFFT_TMA_CASE(6)
+        BFFT_TMA_CASE(7)
+        BFFT_TMA_CASE(8)
+        BFFT_TMA_CASE(9)
+        default: return cudaErrorNotSupported;
+    }
+#undef BFFT_TMA_CASE
+}
+
+}  // namespace bfft
