@@ -453,10 +453,15 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="5a")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the workload's batch: a small case of the same kernels for profiler captures "
+                         "(the line is marked profile_case and is not a bench figure)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.batch is not None:
+        wl.update(batch=int(args.batch), desc=wl["desc"] + f" [profile case: batch {args.batch}]", profile_case=True)
 
     if args.impl == "reference":
         run_reference_arm(args, wl)
@@ -481,6 +486,8 @@ def main() -> None:
             "config": res["config"], "roofline": res["roofline"], "cpu_baseline": cpu, "e2e": res["e2e"],
             "gpu_launches": int(res["launches"]), "clocks": res["clocks"],
         }
+        if wl.get("profile_case"):
+            line["profile_case"] = True
         print(json.dumps(line), flush=True)
     ctx.close()
 

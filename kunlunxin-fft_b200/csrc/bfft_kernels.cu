@@ -811,6 +811,9 @@ cudaError_t launch_pass(int log2l, int layout, int lmap, int smap, const float2*
     if (layout == 1) {  // column tiles: TMA-staged pass when the shape allows it
         const cudaError_t e = launch_pass_tma(log2l, in, out, a, s);
         if (e != cudaErrorNotSupported) return e;
+    } else if (smap != 2) {  // row tiles with row outputs: bulk-copy pass when the shape allows it
+        const cudaError_t e = launch_pass_tma_rows(log2l, in, out, a, s);
+        if (e != cudaErrorNotSupported) return e;
     }
     switch (log2l) {
         case 1: return launch_pass_l<1>(layout, lmap, smap, in, out, a, s);

@@ -14,10 +14,11 @@
 // computes a global address per element; the copies are asynchronous and
 // tracked by mbarriers (loads) and bulk groups (stores).
 //
-// Pipeline: three stages per CTA, persistent over tiles.  While tile i is
-// transformed in stage i % 3, the load of tile i+1 is in flight into stage
-// (i+1) % 3, whose previous contents (tile i-2) the store engine has finished
-// reading.  No multicast: each CTA loads only its own tiles.
+// Pipeline: S stages per CTA (2 for 256-thread CTAs, three of which share an
+// SM; 3 for the 512-thread CTAs of L = 512), persistent over tiles.  While
+// tile i is transformed in stage i % S, the load of tile i+1 is in flight into
+// stage (i+1) % S, whose previous contents (tile i+1-S) the store engine has
+// finished reading.  No multicast: each CTA loads only its own tiles.
 //
 // Every wait on an mbarrier is bounded (kWaitLimitNs of %globaltimer); on
 // expiry the kernel records a status bit (bfft_device_status), waits once
@@ -95,6 +96,12 @@ __device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t 
                  "r"(smem_u32(src)), "r"(bytes)
                  : "memory");
 }
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void bulk_wait_read() {
@@ -122,8 +129,10 @@ struct PassTGeo {
     static constexpr int LB = L < 256 ? L : 256;  // TMA box extent along the element index
     static constexpr int RPAD = ROWS ? 2 : 0;     // row staging: 16-byte aligned rows, 2-way conflicts at most
     static constexpr int SB = ((K * (L + RPAD) * 8) + 1023) / 1024 * 1024;
-    static constexpr int STAGES = 3;
-    static constexpr int MINB = THREADS >= 512 ? 1 : 2;
+    // 256-thread CTAs: two stages and <= 85 registers, three CTAs (24 warps)
+    // per SM; 512-thread CTAs (L = 512): one per SM, three stages.
+    static constexpr int STAGES = THREADS >= 512 ? 3 : 2;
+    static constexpr int MINB = THREADS >= 512 ? 1 : 3;
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * SB + 64 + (size_t)tw_total(LOG2L) * sizeof(float2);
     static_assert(L >= 16 && K <= 256 && LB <= 256, "TMA box limits");
 };
@@ -190,8 +199,8 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
         float2* buf = stage(s);
         const int64_t f = tile * G::K + cl;
         const int64_t o = f >> a.inner_log2, c = f & imask;
-        // the stores that read the stage the next load will fill (tile it-2) are done reading
-        if (tid < NST) bulk_wait_read<1>();
+        // the stores that read the stage the next load will fill (tile it+1-STAGES) are done reading
+        if (tid < NST) bulk_wait_read<G::STAGES - 2>();
         const bool ok = mbar_wait_bounded(&full[s], static_cast<uint32_t>((it / G::STAGES) & 1));
 
         const uint32_t cmul32 = static_cast<uint32_t>(c) * static_cast<uint32_t>(a.tw_mul);
@@ -246,6 +255,155 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
         }
     }
     if (aborted && tid == 0)  // the copy this tile waited for may still land: wait (bounded) before leaving
+        mbar_wait_bounded(&full[it % G::STAGES], static_cast<uint32_t>((it / G::STAGES) & 1));
+    if (tid < NST) bulk_wait<0>();
+}
+
+// ---- row tiles: sub-FFTs whose elements are contiguous (L >= 256) ----
+//
+// A tile is K rows of L points; every row is one bulk copy (one copy for the
+// whole tile when its rows are adjacent) into a dense [row][element] stage,
+// which the element-fastest thread mapping reads without bank conflicts for
+// L >= 256.  The Stockham exchanges then use the padded per-row layout of
+// k_pass in the same stage, and the outputs are staged densely again for
+// bulk copies out.  A partial last tile copies only its rows.
+template <int LOG2L>
+struct PassRGeo {
+    static constexpr int L = 1 << LOG2L;
+    static constexpr int E = 16;
+    static constexpr int TF = L / E;
+    static constexpr int K = 256 / TF;  // 256 threads
+    static constexpr int THREADS = 256;
+    static constexpr int LPAD = (L + (L >> 4)) | 1;
+    static constexpr int SB = ((K * LPAD * 8) + 1023) / 1024 * 1024;
+    static constexpr int STAGES = 2;
+    static constexpr int MINB = 3;
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * SB + 64 + (size_t)tw_total(LOG2L) * sizeof(float2);
+    static_assert(L >= 256 && K >= 1, "row tiles need L >= 256");
+};
+
+template <int LOG2L>
+__global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MINB)
+    k_pass_tma_rows(const float2* __restrict__ in, float2* __restrict__ out, PassArgs a, int in_contig,
+                    int out_contig) {
+    using G = PassRGeo<LOG2L>;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* base =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + G::STAGES * G::SB);
+    float2* tw_smem = reinterpret_cast<float2*>(full + 8);
+    float2* tw2 = tw_smem + tw_total(LOG2L);
+    auto stage = [&](int s) { return reinterpret_cast<float2*>(base + s * G::SB); };
+
+    const int tid = threadIdx.x;
+    const int cl = tid / G::TF, t = tid % G::TF;
+    const int64_t ntiles = (a.nsub + G::K - 1) / G::K;
+    const int64_t imask = (int64_t(1) << a.inner_log2) - 1;
+    const float osr = a.scale, osi = a.conj_out ? -a.scale : a.scale;
+    const int NST = out_contig ? 1 : G::K;  // threads that issue (and wait for) stores
+
+    fill_stockham_twiddles<LOG2L>(tw_smem);
+    const bool tws = a.tw_smem_entries > 0;
+    const int lo_bits = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
+    const uint32_t lo_mask = (1u << lo_bits) - 1u;
+    if (tws) {
+        const int nlo = 1 << lo_bits, nhi = a.tw.log2n > lo_bits ? 1 << (a.tw.log2n - lo_bits) : 0;
+        for (int i = tid; i < nlo; i += blockDim.x) tw2[i] = a.tw.lo[i];
+        for (int i = tid; i < nhi; i += blockDim.x) tw2[nlo + i] = a.tw.hi[i];
+    }
+    const float2* tw2hi = tw2 + (1 << lo_bits);
+    const uint32_t nmask = a.tw.log2n >= 32 ? 0xffffffffu : (1u << a.tw.log2n) - 1u;
+    auto twiddle = [&](uint32_t e) -> float2 {
+        if (!tws) return tw_two_level(a.tw, e);
+        e &= nmask;
+        const float2 w = tw2[e & lo_mask];
+        return a.tw.log2n > lo_bits ? cmul(w, tw2hi[e >> lo_bits]) : w;
+    };
+    auto row_in = [&](int64_t f) -> const float2* {
+        const int64_t o = f >> a.inner_log2, c = f & imask;
+        const int64_t cin = a.in_base_bits ? (int64_t)brev_bits((uint32_t)c, a.in_base_bits) : c;
+        return in + o * a.in_outer + cin * a.in_inner;
+    };
+    auto row_out = [&](int64_t f) -> float2* {
+        const int64_t o = f >> a.inner_log2, c = f & imask;
+        const int64_t cout = a.out_base_bits ? (int64_t)brev_bits((uint32_t)c, a.out_base_bits) : c;
+        return out + o * a.out_outer + cout * a.out_inner;
+    };
+    if (tid == 0) {
+        for (int s = 0; s < G::STAGES; ++s) mbar_init(&full[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_proxy_async_smem();
+    }
+    __syncthreads();
+
+    auto issue = [&](int64_t tl, int s) {  // thread 0 only
+        const int64_t f0 = tl * G::K;
+        const int rows = static_cast<int>(a.nsub - f0 < G::K ? a.nsub - f0 : G::K);
+        float2* dst = stage(s);
+        const uint32_t row_bytes = static_cast<uint32_t>(G::L * sizeof(float2));
+        mbar_arrive_expect_tx(&full[s], row_bytes * rows);
+        if (in_contig) {
+            bulk_load(dst, row_in(f0), row_bytes * rows, &full[s]);
+        } else {
+            for (int r = 0; r < rows; ++r) bulk_load(dst + r * G::L, row_in(f0 + r), row_bytes, &full[s]);
+        }
+    };
+
+    int64_t tile = blockIdx.x;
+    if (tid == 0 && tile < ntiles) issue(tile, 0);
+    int it = 0;
+    bool aborted = false;
+    for (; tile < ntiles; ++it, tile += gridDim.x) {
+        const int s = it % G::STAGES;
+        float2* buf = stage(s);
+        const int64_t f = tile * G::K + cl;
+        const bool active = f < a.nsub;
+        const int64_t c = f & imask;
+        if (tid < NST) bulk_wait_read<G::STAGES - 2>();
+        const bool ok = mbar_wait_bounded(&full[s], static_cast<uint32_t>((it / G::STAGES) & 1));
+
+        const uint32_t cmul32 = static_cast<uint32_t>(c) * static_cast<uint32_t>(a.tw_mul);
+        float2 v[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            const uint32_t e = static_cast<uint32_t>(t + m * G::TF);
+            float2 val = ok ? buf[cl * G::L + e] : make_float2(0.f, 0.f);
+            if (a.conj_in) val.y = -val.y;
+            if (a.tw_mode == 1) val = cmul(val, twiddle(e * cmul32));
+            v[m] = val;
+        }
+        if (__syncthreads_or(!ok)) {
+            aborted = true;
+            break;
+        }
+        if (tid == 0 && tile + gridDim.x < ntiles) issue(tile + gridDim.x, (it + 1) % G::STAGES);
+
+        stockham_passes<LOG2L, 0, 16, G::TF>(v, t, buf + cl * G::LPAD, tw_smem);
+
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            const uint32_t k = static_cast<uint32_t>(t + m * G::TF);
+            float2 val = v[m];
+            if (a.tw_mode == 2) val = cmul(val, twiddle(k * cmul32));
+            buf[cl * G::L + k] = make_float2(val.x * osr, val.y * osi);
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        const int64_t f0 = tile * G::K;
+        const int rows = static_cast<int>(a.nsub - f0 < G::K ? a.nsub - f0 : G::K);
+        const uint32_t row_bytes = static_cast<uint32_t>(G::L * sizeof(float2));
+        if (out_contig) {
+            if (tid == 0) {
+                bulk_store(row_out(f0), buf, row_bytes * rows);
+                bulk_commit();
+            }
+        } else if (tid < G::K) {
+            if (tid < rows) bulk_store(row_out(f0 + tid), buf + tid * G::L, row_bytes);
+            bulk_commit();  // an empty group keeps every storing thread's group count in step
+        }
+        (void)active;
+    }
+    if (aborted && tid == 0)
         mbar_wait_bounded(&full[it % G::STAGES], static_cast<uint32_t>((it / G::STAGES) & 1));
     if (tid < NST) bulk_wait<0>();
 }
@@ -336,6 +494,83 @@ static cudaError_t launch_pass_tma_t(const float2* in, float2* out, const PassAr
     const size_t smem = G::SMEM + (size_t)b.tw_smem_entries * sizeof(float2);
     kern<<<(unsigned)grid, G::THREADS, smem, s>>>(tin, tout, out, b);
     return cudaGetLastError();
+}
+
+template <int LOG2L>
+static cudaError_t launch_pass_tma_rows_t(const float2* in, float2* out, const PassArgs& a, int in_contig,
+                                          int out_contig, cudaStream_t s) {
+    using G = PassRGeo<LOG2L>;
+    auto kern = k_pass_tma_rows<LOG2L>;
+    constexpr int kTw2MaxLog2 = 12;
+    constexpr size_t kSmemCap = 227 * 1024;
+    static int blocks_per_sm[64][kTw2MaxLog2 + 2] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    PassArgs b = a;
+    b.tw_smem_entries = 0;
+    int cls = 0;
+    if (a.tw_mode != 0) {
+        const int lob = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
+        const int nlo = 1 << lob, nhi = a.tw.log2n > lob ? 1 << (a.tw.log2n - lob) : 0;
+        int c = 0;
+        while ((1 << c) < nlo + nhi) ++c;
+        if (c <= kTw2MaxLog2 && G::SMEM + ((size_t)sizeof(float2) << c) <= kSmemCap) {
+            b.tw_smem_entries = nlo + nhi;
+            cls = c + 1;
+        }
+    }
+    const size_t smem_cls = G::SMEM + (cls ? ((size_t)sizeof(float2) << (cls - 1)) : 0);
+    if (blocks_per_sm[dev][cls] == 0) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
+        if (e != cudaSuccess) return e;
+        int nb = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, G::THREADS, smem_cls);
+        if (e != cudaSuccess) return e;
+        if (g_num_sms == 0) {
+            e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess) return e;
+        }
+        blocks_per_sm[dev][cls] = nb > 0 ? nb : 1;
+    }
+    const int64_t ntiles = (b.nsub + G::K - 1) / G::K;
+    int64_t grid = (int64_t)blocks_per_sm[dev][cls] * g_num_sms;
+    if (grid > ntiles) grid = ntiles;
+    if (grid < 1) grid = 1;
+    const size_t smem = G::SMEM + (size_t)b.tw_smem_entries * sizeof(float2);
+    kern<<<(unsigned)grid, G::THREADS, smem, s>>>(in, out, b, in_contig, out_contig);
+    return cudaGetLastError();
+}
+
+// Row tiles through bulk copies when the shapes allow it.
+static cudaError_t launch_pass_tma_rows(int log2l, const float2* in, float2* out, const PassArgs& a,
+                                        cudaStream_t s) {
+    if (log2l < 8 || log2l > 12) return cudaErrorNotSupported;
+    const int64_t L = int64_t(1) << log2l;
+    const int k = 256 / (int)(L / 16);
+    const int64_t inner = int64_t(1) << a.inner_log2;
+    if (((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) || a.in_stride != 1 ||
+        a.out_stride != 1 || a.in_elem_bitrev || a.out_elem_bitrev)
+        return cudaErrorNotSupported;
+    // every row start 16-byte aligned
+    if ((a.in_outer & 1) || (inner > 1 && (a.in_inner & 1)) || (a.out_outer & 1) || (inner > 1 && (a.out_inner & 1)))
+        return cudaErrorNotSupported;
+    // a tile's rows are adjacent in memory: one copy per tile
+    auto contiguous = [&](int64_t outer, int64_t inner_stride, int base_bits) {
+        if (inner == 1) return outer == L;
+        return !base_bits && inner_stride == L && outer == inner * L && inner % k == 0;
+    };
+    const int in_contig = contiguous(a.in_outer, a.in_inner, a.in_base_bits) ? 1 : 0;
+    const int out_contig = contiguous(a.out_outer, a.out_inner, a.out_base_bits) ? 1 : 0;
+    switch (log2l) {
+        case 8: return launch_pass_tma_rows_t<8>(in, out, a, in_contig, out_contig, s);
+        case 9: return launch_pass_tma_rows_t<9>(in, out, a, in_contig, out_contig, s);
+        case 10: return launch_pass_tma_rows_t<10>(in, out, a, in_contig, out_contig, s);
+        case 11: return launch_pass_tma_rows_t<11>(in, out, a, in_contig, out_contig, s);
+        case 12: return launch_pass_tma_rows_t<12>(in, out, a, in_contig, out_contig, s);
+        default: return cudaErrorNotSupported;
+    }
 }
 
 // The TMA pass when the shapes allow it; cudaErrorNotSupported otherwise
