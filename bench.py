@@ -232,12 +232,9 @@ def choose_plan(n: int, b: int):
     p = plan_fft("dit", n, batch=b, profile_hash=DeviceProfile.load().hash())
     if not p.fallback:
         return p, "selector"
-    log2n = n.bit_length() - 1
-    if n <= 4096:
-        tile = n
-    else:  # fewest CTA-resident passes of <= 2^12 points, as equal as possible
-        passes = -(-log2n // 12)
-        tile = 1 << -(-log2n // passes)
+    # one CTA-resident pass up to 4096 points; beyond, a 256-point local group
+    # and tail passes of <= 2^9 points (every pass on the TMA-staged kernels)
+    tile = n if n <= 4096 else 256
     executed = "fft_dit_matrix_batch" if b > 1 else "fft_dit_matrix"
     return ExecutionPlan(n=n, batch=b, direction="dit", precision="fp32", selection_source="table",
                          reason="explicit B200 local-fused core (selector abstained: " + p.reason + ")",

@@ -251,12 +251,17 @@ Step dif_group(int64_t n, int64_t batch, int s0, int g, const TwoLevel& tw) {
     return s;
 }
 
-// Split `count` consecutive stages into the fewest passes of <= kMaxPassLog2
+// Tail passes read and write strided columns; up to 2^9 points they run on
+// the TMA-staged column pass (16 sub-FFTs per tile, 128-byte runs), beyond it
+// on k_pass with shorter runs, which costs more than an extra pass.
+constexpr int kMaxTailPassLog2 = 9;
+
+// Split `count` consecutive stages into the fewest passes of <= kMaxTailPassLog2
 // stages, as equal as possible.
 std::vector<int> split_stages(int count) {
     std::vector<int> out;
     if (count <= 0) return out;
-    int parts = (count + kMaxPassLog2 - 1) / kMaxPassLog2;
+    int parts = (count + kMaxTailPassLog2 - 1) / kMaxTailPassLog2;
     for (int i = 0; i < parts; ++i) out.push_back(count / parts + (i < count % parts ? 1 : 0));
     return out;
 }
