@@ -38,12 +38,19 @@ for _p in (PKG_ROOT, REPO):
 WORKLOADS = {
     "5a": {"n": 65536, "batch": 8192,
            "desc": "config 5a: batch-sharded C2C forward, N=65536, B=8192 (4 GiB complex64) split over ranks"},
+    "sweep": {"n": 4096, "batch": 4096, "desc": "config 3 point: C2C forward, B*N=2^24 (set N with --n)"},
     "sweep-2^12": {"n": 4096, "batch": 4096, "desc": "config 3 point: C2C forward N=4096, B=4096 (B*N=2^24)"},
     "sweep-2^20": {"n": 1 << 20, "batch": 16, "desc": "config 3 point: C2C forward N=2^20, B=16 (B*N=2^24)"},
     "5b": {"n": 1 << 30, "batch": 1, "kind": "4step", "cpu_n": 1 << 20,
            "desc": "config 5b: one C2C forward of N=2^30 (8 GiB complex64); 4-step over ranks with NCCL all-to-all"},
 }
 SEED = 1234
+# DRAM bytes per launch of the dominant kernel, from an ncu capture of a small
+# case of the same flow scaled by the elements processed (the summary under
+# profiles/ gives the command and the raw figures).  Keyed by workload and plan.
+PROFILED_TRAFFIC = {
+    ("5a", "fft_dit_matrix_batch", 256): (7.83e9, "profiles/k_pass_tma_5a.md"),
+}
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -348,9 +355,12 @@ def run_batch(args, wl, ctx) -> dict:
     per_launch_ms = ms_step / max(native.launches, 1)
     bytes_per_launch = 16.0 * n * b
     achieved = bytes_per_launch / (per_launch_ms / 1e3) / 1e9
-    roofline = {"bound": "hbm", "kernel": "k_pass (CTA-resident Stockham pass)", "achieved": achieved,
+    traffic = PROFILED_TRAFFIC.get((args.workload, plan.executed, int((plan.params or {}).get("tile", 0))))
+    # per launch on this rank (b of the workload's rows), like `achieved`
+    traffic = traffic[0] * b / wl["batch"] if traffic is not None and args.batch is None else None
+    roofline = {"bound": "hbm", "kernel": "k_pass_tma / k_pass (CTA-resident Stockham pass)", "achieved": achieved,
                 "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
-                "traffic": None, "launches_per_step": native.launches,
+                "traffic": traffic, "launches_per_step": native.launches,
                 "algorithmic_bytes_per_launch": bytes_per_launch,
                 "transform_hbm_gbs": 16.0 * n * b / (ms_step / 1e3) / 1e9}
 
@@ -450,6 +460,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="5a")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--n", type=int, default=None,
+                    help="sweep workload: transform length N (power of two <= 2^24), batch 2^24 / N")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the workload's batch: a small case of the same kernels for profiler captures "
                          "(the line is marked profile_case and is not a bench figure)")
@@ -457,6 +469,11 @@ def main() -> None:
     if args.warmup < 3:
         args.warmup = 3
     wl = dict(WORKLOADS[args.workload])
+    if args.n is not None:
+        if args.workload != "sweep" or args.n < 2 or args.n & (args.n - 1) or args.n > (1 << 24):
+            raise SystemExit("--n needs --workload sweep and a power of two in [2, 2^24]")
+        wl.update(n=args.n, batch=(1 << 24) // args.n,
+                  desc=f"config 3 point: C2C forward N={args.n}, B={(1 << 24) // args.n} (B*N=2^24)")
     if args.batch is not None:
         wl.update(batch=int(args.batch), desc=wl["desc"] + f" [profile case: batch {args.batch}]", profile_case=True)
 
