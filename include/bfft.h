@@ -221,6 +221,24 @@ BFFT_EXPORT bfft_status bfft_dist_phase(bfft_dist_plan_t plan, int32_t phase, co
 BFFT_EXPORT bfft_status bfft_dist_plan_launches(bfft_dist_plan_t plan, int32_t phase, int* launches);
 BFFT_EXPORT bfft_status bfft_dist_plan_destroy(bfft_dist_plan_t plan);
 
+/* Host-to-host execution -- no counterpart in the reference (its operator API
+ * takes device tensors).  A stream plan runs `chunks` back-to-back executions
+ * of the plan described by `chunk_desc` (batch = rows per chunk) over host
+ * arrays of chunks * batch rows, overlapping the copy in of chunk k+1, the
+ * transform of chunk k and the copy out of chunk k-1 on three internal
+ * streams with two device buffers per direction (allocated at creation).
+ * bfft_stream_execute orders itself after the work already enqueued on
+ * `stream` and makes `stream` wait for its completion; host buffers should be
+ * page-locked for the copies to overlap.  Shapes per row as in bfft_execute. */
+typedef struct bfft_stream_plan_s* bfft_stream_plan_t;
+BFFT_EXPORT bfft_status bfft_stream_plan_create(const bfft_plan_desc* chunk_desc, int64_t chunks,
+                                                bfft_stream_plan_t* plan);
+BFFT_EXPORT bfft_status bfft_stream_plan_info(bfft_stream_plan_t plan, size_t* in_bytes_per_chunk,
+                                              size_t* out_bytes_per_chunk, int* launches_per_chunk);
+BFFT_EXPORT bfft_status bfft_stream_execute(bfft_stream_plan_t plan, const void* host_in, void* host_out,
+                                            void* stream);
+BFFT_EXPORT bfft_status bfft_stream_plan_destroy(bfft_stream_plan_t plan);
+
 /* Status bits the kernels set on `device` when a bounded wait expired
  * (bit 0: a TMA pass gave up waiting for a tile copy and returned early, so
  * its output is incomplete).  Synchronises the device; clear != 0 resets the

@@ -31,7 +31,8 @@ EXPORTS = ("bfft_api_version", "bfft_last_error", "bfft_plan_create", "bfft_plan
            "bfft_r2c_stitch", "bfft_c2r_pre", "bfft_c2r_unpack", "bfft_twiddle_table",
            "bfft_index_map", "bfft_launch_counter", "bfft_hybrid_c2c_noalloc",
            "bfft_dist_batch_shard", "bfft_dist_plan_create", "bfft_dist_workspace_size",
-           "bfft_dist_phase", "bfft_dist_plan_launches", "bfft_dist_plan_destroy", "bfft_device_status")
+           "bfft_dist_phase", "bfft_dist_plan_launches", "bfft_dist_plan_destroy", "bfft_device_status",
+           "bfft_stream_plan_create", "bfft_stream_plan_info", "bfft_stream_execute", "bfft_stream_plan_destroy")
 
 
 class PlanDesc(ctypes.Structure):
@@ -90,6 +91,10 @@ def load() -> ctypes.CDLL:
         L.bfft_dist_plan_launches.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_int)]
         L.bfft_dist_plan_destroy.argtypes = [vp]
         L.bfft_device_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint32), i32]
+        L.bfft_stream_plan_create.argtypes = [ctypes.POINTER(PlanDesc), i64, ctypes.POINTER(vp)]
+        L.bfft_stream_plan_info.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz), ctypes.POINTER(ctypes.c_int)]
+        L.bfft_stream_execute.argtypes = [vp, vp, vp, vp]
+        L.bfft_stream_plan_destroy.argtypes = [vp]
         for name in EXPORTS:
             fn = getattr(L, name)
             if name not in ("bfft_api_version", "bfft_last_error", "bfft_launch_counter"):
@@ -189,6 +194,34 @@ class NativeDistPlan:
     def phase(self, phase: int, in_ptr: int, out_ptr: int, ws_ptr: int, ws_bytes: int, stream: int) -> None:
         check(load().bfft_dist_phase(self.handle, int(phase), in_ptr, out_ptr, ws_ptr, ws_bytes, stream),
               "bfft_dist_phase")
+
+
+def _destroy_stream(handle: int) -> None:
+    try:
+        if _lib is not None and handle:
+            _lib.bfft_stream_plan_destroy(ctypes.c_void_p(handle))
+    except Exception:  # noqa: BLE001 - interpreter shutdown
+        pass
+
+
+class NativeStreamPlan:
+    """Owns one bfft_stream_plan_t (host-to-host pipelined execution)."""
+
+    def __init__(self, chunk_desc: PlanDesc, chunks: int):
+        L = load()
+        h = ctypes.c_void_p()
+        check(L.bfft_stream_plan_create(ctypes.byref(chunk_desc), int(chunks), ctypes.byref(h)),
+              "bfft_stream_plan_create")
+        self.handle = h.value
+        self.chunks = int(chunks)
+        ib, ob, nl = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_int()
+        check(L.bfft_stream_plan_info(self.handle, ctypes.byref(ib), ctypes.byref(ob), ctypes.byref(nl)),
+              "bfft_stream_plan_info")
+        self.in_bytes, self.out_bytes, self.launches_per_chunk = int(ib.value), int(ob.value), int(nl.value)
+        self._fin = weakref.finalize(self, _destroy_stream, self.handle)
+
+    def execute(self, host_in: int, host_out: int, stream: int) -> None:
+        check(load().bfft_stream_execute(self.handle, host_in, host_out, stream), "bfft_stream_execute")
 
 
 def batch_shard(batch: int, nranks: int, rank: int) -> tuple[int, int]:

@@ -406,16 +406,53 @@ def test_tma_passes_odd_batches(n, tiles):
     the rows per tile) and the TMA column pass (every tail pass, strided local
     groups), both directions, forward and ortho inverse."""
     rng = np.random.default_rng(n)
-    for b in (1, 3, 17):
+    for b in (1, 2, 8):  # the runner functions take power-of-two batches (the reference's rule)
         x = cplx(rng, (b, n))
         t = dev(x)
         for tile in tiles:
             for name in ("fft_dit_matrix_batch", "fft_dif_matrix_batch"):
                 got = host(getattr(runner, name)(t, tile=tile)).reshape(b, n)
                 assert rel_l2_per_transform(got, _f64(x)) <= TOL_F64, (name, n, b, tile)
+    for b in (1, 3, 17):  # plans take any batch
+        x = cplx(rng, (b, n))
+        t = dev(x)
+        for tile in tiles:
+            fwd = _plan("fft_dif_matrix_batch", n, b, params={"tile": tile})
+            got = host(execute_fft_plan(fwd, t if b > 1 else t[0])).reshape(b, n)
+            assert rel_l2_per_transform(got, _f64(x)) <= TOL_F64, (n, b, tile, "dif")
             p = _plan("fft_dit_matrix_batch", n, b, params={"tile": tile}, transform_direction="inverse",
                       norm="ortho")
             y = host(execute_fft_plan(p, t if b > 1 else t[0])).reshape(b, n)
             ref = np.fft.ifft(x.astype(np.complex128), norm="ortho")
             assert rel_l2_per_transform(y, ref) <= TOL_F64, (n, b, tile, "inverse")
     assert _lib.device_status(0) == 0
+
+
+@pytest.mark.parametrize("n, b, tt, chunks", [(1024, 64, "c2c", 4), (65536, 32, "c2c", 8), (4096, 16, "r2c", 4),
+                                             (4096, 16, "c2r", 2), (2048, 1, "c2c", 1)])
+def test_host_buffer_execution(n, b, tt, chunks):
+    """execute_fft_plan_host (chunked, copies overlapped with the transform on
+    three streams) equals the device path bit for bit and float64 within
+    tolerance."""
+    from bfft.host_io import execute_fft_plan_host
+
+    rng = np.random.default_rng(n + b)
+    if tt == "r2c":
+        x = rng.standard_normal((b, n)).astype(np.float32)
+        ref = np.fft.rfft(x.astype(np.float64))
+        p = _plan("fft_dif_matrix_batch", n, b, params={"tile": n // 2, "real_flow": "dedicated-r2c-pack-v1"},
+                  transform_type="r2c")
+    elif tt == "c2r":
+        x = np.fft.rfft(rng.standard_normal((b, n))).astype(np.complex64)
+        ref = np.fft.irfft(x.astype(np.complex128), n=n)
+        p = _plan("fft_dit_matrix_batch", n, b, params={"tile": n // 2, "real_flow": "dedicated-c2r-hermitian-v1"},
+                  transform_type="c2r", transform_direction="inverse")
+    else:
+        x = cplx(rng, (b, n))
+        ref = np.fft.fft(x.astype(np.complex128))
+        p = _plan("fft_dit_matrix_batch" if b > 1 else "fft_dit_matrix", n, b, params={"tile": min(n, 256)})
+    xt = torch.from_numpy(x if b > 1 else x[0]).pin_memory()
+    got = execute_fft_plan_host(p, xt, chunks=chunks).numpy()
+    dev_out = host(execute_fft_plan(p, xt.cuda()))
+    assert np.array_equal(got, dev_out)
+    assert rel_l2_per_transform(got.reshape(ref.shape), ref) <= TOL_F64
