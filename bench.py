@@ -41,6 +41,14 @@ WORKLOADS = {
     "sweep": {"n": 4096, "batch": 4096, "desc": "config 3 point: C2C forward, B*N=2^24 (set N with --n)"},
     "sweep-2^12": {"n": 4096, "batch": 4096, "desc": "config 3 point: C2C forward N=4096, B=4096 (B*N=2^24)"},
     "sweep-2^20": {"n": 1 << 20, "batch": 16, "desc": "config 3 point: C2C forward N=2^20, B=16 (B*N=2^24)"},
+    "c1": {"n": 2048, "batch": 1, "desc": "config 1: single C2C forward FFT, N=2048, B=1 (rank-1)"},
+    "c2-fwd": {"n": 2048, "batch": 64, "desc": "config 2: batched C2C forward, N=2048, B=64"},
+    "c2-inv": {"n": 2048, "batch": 64, "td": "inverse",
+               "desc": "config 2: batched C2C inverse (1/N), N=2048, B=64"},
+    "c4-r2c": {"n": 65536, "batch": 256, "tt": "r2c",
+               "desc": "config 4: R2C forward, N=65536, B=256 (float32 in, half spectrum out)"},
+    "c4-c2r": {"n": 65536, "batch": 256, "tt": "c2r", "td": "inverse",
+               "desc": "config 4: C2R inverse, N=65536, B=256 (half spectrum in, float32 out)"},
     "5b": {"n": 1 << 30, "batch": 1, "kind": "4step", "cpu_n": 1 << 20,
            "desc": "config 5b: one C2C forward of N=2^30 (8 GiB complex64); 4-step over ranks with NCCL all-to-all"},
 }
@@ -228,17 +236,29 @@ def run_reference_arm(args, wl) -> None:
 
 # ------------------------------------------------------------------ GPU arm
 
-def choose_plan(n: int, b: int):
+def choose_plan(n: int, b: int, tt: str = "c2c", td: str = "forward"):
     """The plan the public API resolves for this shape; when the table
-    abstains (no B200 table bound to this environment) use the B200 batch
-    local-fused core explicitly and say so."""
+    abstains (no B200 table bound to this environment, or a shape outside its
+    matrix) use the B200 local-fused core explicitly and say so."""
     from bfft import plan_fft
     from bfft.config import DeviceProfile
     from bfft.entry import ExecutionPlan
 
-    p = plan_fft("dit", n, batch=b, profile_hash=DeviceProfile.load().hash())
+    p = plan_fft("dit", n, batch=b, profile_hash=DeviceProfile.load().hash(), transform_type=tt,
+                 transform_direction=td)
     if not p.fallback:
         return p, "selector"
+    if tt != "c2c":
+        real_flow = "dedicated-r2c-pack-v1" if tt == "r2c" else "dedicated-c2r-hermitian-v1"
+        half = n // 2
+        return ExecutionPlan(n=n, batch=b, direction="dit", precision="fp32", selection_source="table",
+                             reason="explicit B200 dedicated real flow (selector abstained: " + p.reason + ")",
+                             fallback=False, executed="fft_dit_matrix_batch" if b > 1 else "fft_dit_matrix",
+                             block=256, flow_id=real_flow, flow_realization="matrix-resident",
+                             processing_unit="dense-dot-fft64",
+                             params={"tile": half if half <= 4096 else 256, "rows": 1, "variant": "spread",
+                                     "batch": b, "real_flow": real_flow},
+                             transform_type=tt, transform_direction=td), "explicit"
     # one CTA-resident pass up to 4096 points; beyond, a 256-point local group
     # and tail passes of <= 2^9 points (every pass on the TMA-staged kernels)
     tile = n if n <= 4096 else 256
@@ -248,7 +268,8 @@ def choose_plan(n: int, b: int):
                          fallback=False, executed=executed, block=256,
                          flow_id="local-fused-tile", flow_realization="matrix-resident",
                          processing_unit="dense-dot-fft64",
-                         params={"tile": tile, "rows": 1, "variant": "spread", "batch": b}), "explicit"
+                         params={"tile": tile, "rows": 1, "variant": "spread", "batch": b},
+                         transform_direction=td), "explicit"
 
 
 class Ctx:
@@ -285,24 +306,42 @@ class Ctx:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
-    def timed(self, fn, steps: int):
-        """(max-over-ranks ms of `steps` calls of fn, launches, clocks)."""
+    def timed(self, fn, steps: int, flush_l2: bool = False):
+        """(max-over-ranks ms of `steps` calls of fn, launches, clocks).
+
+        flush_l2: inputs smaller than L2 -- before every step a 256 MiB buffer
+        is written (outside the timed spans) and only the call is timed."""
         from bfft import _lib
 
         torch = self.torch
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=self.dev) if flush_l2 else None
         self.barrier()
         l0 = _lib.launch_counter()
         with ClockSampler(self.local) as clk:
-            start = torch.cuda.Event(enable_timing=True)
-            end = torch.cuda.Event(enable_timing=True)
-            start.record(self.stream)
-            for _ in range(steps):
-                fn()
-            end.record(self.stream)
-            end.synchronize()
+            if flush is None:
+                start = torch.cuda.Event(enable_timing=True)
+                end = torch.cuda.Event(enable_timing=True)
+                start.record(self.stream)
+                for _ in range(steps):
+                    fn()
+                end.record(self.stream)
+                end.synchronize()
+                ms = start.elapsed_time(end)
+            else:
+                spans = []
+                for _ in range(steps):
+                    flush.fill_(1)
+                    a = torch.cuda.Event(enable_timing=True)
+                    b = torch.cuda.Event(enable_timing=True)
+                    a.record(self.stream)
+                    fn()
+                    b.record(self.stream)
+                    spans.append((a, b))
+                spans[-1][1].synchronize()
+                ms = sum(a.elapsed_time(b) for a, b in spans)
             self.barrier()
         launches = _lib.launch_counter() - l0
-        return self.max_over_ranks(start.elapsed_time(end)), launches, clk.summary()
+        return self.max_over_ranks(ms), launches, clk.summary()
 
     def close(self):
         if self.world > 1:
@@ -336,24 +375,38 @@ def run_batch(args, wl, ctx) -> dict:
 
     torch = ctx.torch
     n, btot = wl["n"], wl["batch"]
+    tt, td = wl.get("tt", "c2c"), wl.get("td", "forward")
     first, b = bdist.batch_shard(btot, ctx.world, ctx.rank)
-    plan, plan_src = choose_plan(n, b)
+    plan, plan_src = choose_plan(n, b, tt, td)
     g = torch.Generator(device=ctx.dev).manual_seed(SEED + ctx.rank)
-    x = torch.complex(torch.randn(b, n, device=ctx.dev, generator=g), torch.randn(b, n, device=ctx.dev, generator=g))
+    if tt == "r2c":
+        x = torch.randn(b, n, device=ctx.dev, generator=g)
+    else:
+        cols = n // 2 + 1 if tt == "c2r" else n
+        x = torch.complex(torch.randn(b, cols, device=ctx.dev, generator=g),
+                          torch.randn(b, cols, device=ctx.dev, generator=g))
+    if b == 1:
+        x = x[0].contiguous()
+    # algorithmic bytes and flops of one step (real transforms: 2.5 N log2 N)
+    in_row = 4 * n if tt == "r2c" else 8 * (n // 2 + 1) if tt == "c2r" else 8 * n
+    out_row = 8 * (n // 2 + 1) if tt == "r2c" else 4 * n if tt == "c2r" else 8 * n
+    flop_scale = 0.5 if tt != "c2c" else 1.0
     torch.cuda.synchronize(ctx.dev)
     for _ in range(args.warmup):
         y = bfft.execute_fft_plan(plan, x)
     del y
     native = native_plan_for(plan, ctx.local)
-    elapsed_ms, launches, clocks = ctx.timed(lambda: bfft.execute_fft_plan(plan, x), args.steps)
+    small = in_row * b < (126 << 20)  # smaller than L2: flush between timed steps
+    elapsed_ms, launches, clocks = ctx.timed(lambda: bfft.execute_fft_plan(plan, x), args.steps, flush_l2=small)
     ms_step = elapsed_ms / args.steps
-    value = gflop(n, btot) / (ms_step / 1e3)
+    value = flop_scale * gflop(n, btot) / (ms_step / 1e3)
 
     # dominant kernel: every launch of this flow is the CTA-resident pass (or
-    # the cluster kernel); each moves one read + one write of the shard
+    # the cluster kernel); each moves one read + one write of the shard (real
+    # flows: the whole flow's algorithmic bytes over its launches)
     peak, peak_src = measured_peaks()
     per_launch_ms = ms_step / max(native.launches, 1)
-    bytes_per_launch = 16.0 * n * b
+    bytes_per_launch = float((in_row + out_row) * b) if tt != "c2c" else 16.0 * n * b
     achieved = bytes_per_launch / (per_launch_ms / 1e3) / 1e9
     traffic = PROFILED_TRAFFIC.get((args.workload, plan.executed, int((plan.params or {}).get("tile", 0))))
     # per launch on this rank (b of the workload's rows), like `achieved`
@@ -362,15 +415,16 @@ def run_batch(args, wl, ctx) -> dict:
                 "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
                 "traffic": traffic, "launches_per_step": native.launches,
                 "algorithmic_bytes_per_launch": bytes_per_launch,
-                "transform_hbm_gbs": 16.0 * n * b / (ms_step / 1e3) / 1e9}
+                "transform_hbm_gbs": (in_row + out_row) * b / (ms_step / 1e3) / 1e9}
 
     # end to end: host (pinned) in, host out, through the public host-buffer
     # entry; every step copies its input in and its result out
     from bfft.host_io import default_chunks, execute_fft_plan_host
 
-    xh = torch.empty((b, n), dtype=torch.complex64, pin_memory=True)
+    xh = torch.empty(tuple(x.shape), dtype=x.dtype, pin_memory=True)
     xh.copy_(x)
-    yh = torch.empty((b, n), dtype=torch.complex64, pin_memory=True)
+    oshape = (*x.shape[:-1], n // 2 + 1 if tt == "r2c" else n)
+    yh = torch.empty(oshape, dtype=torch.float32 if tt == "c2r" else torch.complex64, pin_memory=True)
     del x
     chunks = default_chunks(plan)
     steps = args.e2e_steps or max(1, min(args.steps, 5))
@@ -385,16 +439,20 @@ def run_batch(args, wl, ctx) -> dict:
     e2.synchronize()
     ctx.barrier()
     e2e_ms = ctx.max_over_ranks(s2.elapsed_time(e2)) / steps
-    e2e = {"value": gflop(n, btot) / (e2e_ms / 1e3), "unit": "GFLOP/s", "ms_per_step": e2e_ms,
-           "h2d_bytes_per_step": int(xh.numel() * 8) * ctx.world, "d2h_bytes_per_step": int(yh.numel() * 8) * ctx.world,
+    e2e = {"value": flop_scale * gflop(n, btot) / (e2e_ms / 1e3), "unit": "GFLOP/s", "ms_per_step": e2e_ms,
+           "h2d_bytes_per_step": int(xh.numel() * xh.element_size()) * ctx.world,
+           "d2h_bytes_per_step": int(yh.numel() * yh.element_size()) * ctx.world,
            "chunks": chunks,
            "path": "execute_fft_plan_host (bfft public API -> libbfft bfft_stream_execute): pinned host in/out, "
                    "batch in chunks, copy in / transform / copy out overlapped on three streams"}
     return {"value": value, "ms_step": ms_step, "launches": launches, "clocks": clocks, "roofline": roofline,
             "e2e": e2e, "scaling": "strong",
             "config": {"workload": wl["desc"], "n": n, "global_batch": btot, "per_rank_batch": b,
+                       "transform": f"{tt}/{td}", "flop_convention": "5 N log2 N" if tt == "c2c" else "2.5 N log2 N",
                        "parallelism": f"batch-shard x{ctx.world} (no data-path collective)",
-                       "l2": "inputs larger than L2 (8 B * N * B per rank >= 512 MiB)",
+                       "l2": ("inputs larger than L2" if not small
+                              else "input smaller than L2: a 256 MiB buffer is written before every step, "
+                                   "only the call is timed"),
                        "plan": plan.executed, "plan_params": plan.params, "plan_source": plan_src},
             "gflop_per_step": gflop(n, btot)}
 

@@ -190,11 +190,11 @@ bfft_status make_row_plan(int64_t n, int64_t batch, int32_t tile, int32_t device
     if (tile > 0) {
         d.tile = tile;
     } else {
-        // Whole rows on chip when they fit (one CTA up to 2^12 points, one
-        // thread-block cluster for 2^13..2^16), else a local group of about
-        // half the stages followed by the tail passes.
+        // Whole rows on chip up to 2^12 points (one CTA), else a 256-point
+        // local group and tail passes of <= 2^9 points, every pass on the
+        // TMA-staged kernels (faster than the cluster kernel on batches).
         const int l = ilog2(n);
-        d.tile = (l <= kMaxPassLog2 || cluster_supported(l)) ? (int32_t)n : (int32_t)((int64_t)1 << ((l + 1) / 2));
+        d.tile = l <= kMaxPassLog2 ? (int32_t)n : 256;
     }
     d.rows = 1;
     d.glog = 4;
