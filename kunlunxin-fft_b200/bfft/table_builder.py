@@ -165,6 +165,18 @@ def candidates(shape: Shape, space: DesignSpace | None = None) -> tuple[dict, li
     if b == 1 and n >= 256:
         cands[f"m3_g_{d}_t64"] = _desc("local-fused-tile", "grouped-boundary", "composite-linear-map",
                                        {"tile": 64, "glog": 4, "maxp": 65536, "cells": 1})
+    # exact-shape composition candidates (the 4-step run_hybrid flow, both
+    # factors CTA-resident): measured beside the table candidates, promoted
+    # only through the composition table (compose), never a table entry
+    if d == "dit" and shape.transform_type == "c2c" and shape.transform_direction == "forward" \
+            and shape.normalization == "backward" and not shape.semantic:
+        t = max(16, n // 4096)
+        while t <= min(4096, n // 16):
+            cands[f"hyb_t{t}"] = {"block": 256, "flow_id": "hybrid-4step",
+                                  "flow_realization": "decomposition-composition",
+                                  "processing_unit": "b200-pass-subfft", "params": {"tile": t, "core": "b200-pass"},
+                                  "executed": "run_hybrid", "composition": True}
+            t *= 2
     return cands, incumbents
 
 
@@ -175,6 +187,8 @@ def _plan_of(shape: Shape, desc: dict):
 
     params = dict(desc["params"])
     name = desc.get("executed")
+    if desc.get("composition"):
+        params["flow_kind"] = "composition"
     if name is None:
         sel = Selection(n=shape.n, direction=shape.direction, batch=shape.batch, precision="fp32", source="table",
                         reason="candidate", block=desc["block"], flow_id=desc["flow_id"],
@@ -301,6 +315,30 @@ def measure(shapes: list[Shape] | None = None, *, sessions: int = 3, trials: int
             c["sessions"] = len(c["session_medians_ms"])
             c["median_ms"] = statistics.median(c["session_medians_ms"]) if c["session_medians_ms"] else None
             c["complete"] = c["sessions"] == sessions and c["n_trials"] == sessions * trials
+        # independent confirmation session: the best composition candidate and
+        # the best table candidate, timed again after the search sessions
+        conf = {}
+        for comp in (True, False):
+            pool = [(c["median_ms"], k) for k, c in rec["candidates"].items()
+                    if c["median_ms"] and bool(c["descriptor"].get("composition")) == comp]
+            if not pool:
+                continue
+            name = min(pool)[1]
+            times = []
+            for _ in range(trials):
+                st = torch.cuda.Event(enable_timing=True)
+                en = torch.cuda.Event(enable_timing=True)
+                torch.cuda._sleep(_spin_cycles())
+                st.record(stream)
+                execute_fft_plan(plans[name], x)
+                en.record(stream)
+                en.synchronize()
+                times.append(st.elapsed_time(en))
+            times.sort()
+            p50 = statistics.median(times)
+            conf[name] = {"p50_ms": p50, "mad_ms": statistics.median(abs(t - p50) for t in times),
+                          "p95_ms": times[min(len(times) - 1, int(0.95 * len(times)))], "trials": len(times)}
+        rec["confirmation"] = conf
         out_shapes.append(rec)
         if log:
             best = min((c["median_ms"], k) for k, c in rec["candidates"].items() if c["median_ms"])
@@ -397,6 +435,8 @@ def build_table(runs: list[dict], *, guard_pct: float = GUARD_PCT, sources: list
         s = shapes[key]
         verdicts = {}
         for name in s.get("candidates") or {}:
+            if s["candidates"][name]["descriptor"].get("composition"):
+                continue  # promoted only through the composition table
             ms, why = candidate_verdict(s, name, threshold=thr, sessions=ns, trials=nt)
             if why:
                 rejections.append(why)
@@ -446,6 +486,107 @@ def build_table(runs: list[dict], *, guard_pct: float = GUARD_PCT, sources: list
     return table
 
 
+# ---------------------------------------------------------------- composition promotion
+
+def _git_commit() -> str:
+    import subprocess
+
+    try:
+        return subprocess.run(["git", "rev-parse", "HEAD"], capture_output=True, text=True, timeout=10,
+                              cwd=os.path.dirname(os.path.abspath(__file__))).stdout.strip() or "unknown"
+    except Exception:  # noqa: BLE001
+        return "unknown"
+
+
+def build_composition_table(runs: list[dict], selector_table: dict, *, guard_pct: float = GUARD_PCT,
+                            sources: list[str] | None = None) -> tuple[dict | None, list[str]]:
+    """Exact-shape composition promotions (the reference's composition
+    registry, src/xpu/composition.py:59-240, config/composition_table.json).
+
+    For every measured c2c shape the incumbent is the lowering the selector
+    table chose for it (M0 / the faster M4 variant when the table has no
+    entry), timed in the same run; the best admissible 4-step candidate is
+    promoted when it beats the incumbent by at least the guard in the search
+    sessions and was re-timed in the independent confirmation session.
+    Returns (table or None when nothing is promoted, verdict lines)."""
+    from . import _build
+    from .composition import KIND, rows_sha256, table_violations
+    from .selector import find_entry
+
+    base = runs[0]["manifest"]
+    thr, ns, nt = float(base["correctness_threshold"]), int(base["sessions"]), int(base["trials"])
+    names = sources or [f"run{i}" for i in range(len(runs))]
+    notes, entries = [], []
+    for ri, run in enumerate(runs):
+        if any(run["manifest"].get(k) != base.get(k) for k in MANIFEST_KEYS):
+            notes.append(f"run {ri}: manifest differs from run 0; refused")
+            continue
+        for s in run["shapes"]:
+            comps = [k for k, c in s["candidates"].items() if c["descriptor"].get("composition")]
+            if not comps:
+                continue
+            key = s["key"]
+            e = find_entry(selector_table, s["n"], s["batch"], s["direction"])
+            if e is not None and e.get("evidence"):
+                inc = e["evidence"]["challenger"].split("@")[0]
+            else:
+                incs = [(s["candidates"][i]["median_ms"], i) for i in s.get("incumbents") or ()
+                        if s["candidates"].get(i, {}).get("median_ms")]
+                inc = min(incs)[1] if incs else None
+            inc_ms, why = (None, "no incumbent") if inc is None else \
+                candidate_verdict(s, inc, threshold=thr, sessions=ns, trials=nt)
+            if why:
+                notes.append(f"{key}: incumbent {inc}: {why}; no promotion")
+                continue
+            best = None
+            for k in comps:
+                ms, why = candidate_verdict(s, k, threshold=thr, sessions=ns, trials=nt)
+                if why:
+                    notes.append(why)
+                elif best is None or ms < best[0]:
+                    best = (ms, k)
+            if best is None:
+                continue
+            gain = (inc_ms - best[0]) / inc_ms * 100.0
+            conf = (s.get("confirmation") or {}).get(best[1])
+            if gain < guard_pct:
+                notes.append(f"{key}: best 4-step {best[1]} {best[0]:.4f} ms vs incumbent {inc} {inc_ms:.4f} ms "
+                             f"({gain:+.1f}% < {guard_pct}%); not promoted")
+                continue
+            if not conf:
+                notes.append(f"{key}: {best[1]} passes the guard but has no confirmation session; not promoted")
+                continue
+            c = s["candidates"][best[1]]
+            entries.append({
+                "N": s["n"], "batch": s["batch"], "direction": "dit", "precision": "fp32",
+                "tile": int(c["descriptor"]["params"]["tile"]), "core": "b200-pass", "flow_id": "hybrid-4step",
+                "flow_realization": "decomposition-composition", "processing_unit": "b200-pass-subfft",
+                "candidate_ms": best[0], "incumbent_ms": inc_ms, "incumbent_flow": inc,
+                "guard_pct": guard_pct_value(best[0], inc_ms), "guard_pass": True,
+                "reason": f"exact-shape 4-step {best[1]} {best[0]:.4f} ms vs table winner {inc} {inc_ms:.4f} ms "
+                          f"(+{gain:.1f}%)",
+                "evidence": {"artifact": names[ri], "artifact_sha256": _sha256_of(run), "commit": _git_commit(),
+                             "sessions": ns, "trials": nt, "confirmation_session": True, "err_max": c["err_max"],
+                             "p50_ms": conf["p50_ms"], "mad_ms": conf["mad_ms"], "p95_ms": conf["p95_ms"]}})
+            notes.append(f"{key}: promoted {best[1]} (+{gain:.1f}% over {inc})")
+    if not entries:
+        return None, notes
+    table = {"schema_version": 1, "kind": KIND, "profile_hash": base["profile_hash"], "env_hash": base["env_hash"],
+             "precision": "fp32", "guard_pct": guard_pct, "contract_id": "b200_pass_core", "entries": entries,
+             "source_hash": _build.source_hash(), "result_sha256": rows_sha256({"rows": entries}),
+             "created": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime())}
+    bad = table_violations(table)
+    if bad:
+        raise ConfigError(f"built composition table violates its contract ({len(bad)}): " + "; ".join(bad[:6]))
+    return table, notes
+
+
+def guard_pct_value(candidate_ms: float, incumbent_ms: float) -> float:
+    from .composition import guard_pct_of
+
+    return guard_pct_of(candidate_ms, incumbent_ms)
+
+
 # ---------------------------------------------------------------- run files
 
 def save_run(run: dict, path: str) -> None:
@@ -485,6 +626,11 @@ def main(argv=None) -> int:
     b.add_argument("runs", nargs="+")
     b.add_argument("--out", default=TABLE_PATH)
     b.add_argument("--guard-pct", type=float, default=GUARD_PCT)
+    c = sub.add_parser("compose", help="promote exact-shape 4-step compositions from run files")
+    c.add_argument("runs", nargs="+")
+    c.add_argument("--selector", default=TABLE_PATH)
+    c.add_argument("--out", default=None)
+    c.add_argument("--guard-pct", type=float, default=GUARD_PCT)
     a = ap.parse_args(argv)
     if a.cmd == "measure":
         run = measure(default_shapes(a.quick), sessions=a.sessions, trials=a.trials, warmup=a.warmup,
@@ -492,6 +638,23 @@ def main(argv=None) -> int:
         save_run(run, a.out)
         return 0
     runs = [load_run(p) for p in a.runs]
+    if a.cmd == "compose":
+        from .composition import TABLE_PATH as COMP_PATH
+        from .selector import load_table
+
+        table, notes = build_composition_table(runs, load_table(a.selector), guard_pct=a.guard_pct,
+                                               sources=[os.path.basename(p) for p in a.runs])
+        for line in notes:
+            print(line)
+        out = a.out or COMP_PATH
+        if table is None:
+            print(f"no composition promoted; {out} not written")
+            return 0
+        with open(out, "w") as f:
+            json.dump(table, f, indent=1)
+            f.write("\n")
+        print(f"{len(table['entries'])} composition entries -> {out}")
+        return 0
     table = build_table(runs, guard_pct=a.guard_pct, sources=[os.path.basename(p) for p in a.runs])
     with open(a.out, "w") as f:
         json.dump(table, f, indent=1)

@@ -30,3 +30,9 @@ def test_measure_and_build_small_matrix():
                      transform_direction=e.get("transform_direction", "forward"),
                      normalization=e.get("normalization", "backward"))
         assert sel.selected, sel.reason
+    comp, notes = TB.build_composition_table([run], t)
+    assert notes  # every c2c shape with 4-step candidates gets a verdict
+    if comp is not None:
+        from bfft.composition import table_violations
+
+        assert table_violations(comp) == []

@@ -47,8 +47,12 @@ def test_candidate_enumeration_matches_the_design_space():
     assert inc == ["m4_spread_dit", "m4_folded_dit"] and "m2_dit_t1024" in c and "m2_dit_t1048576" not in c
     c, inc = TB.candidates(TB.Shape(4096, 256, "dit", "r2c", "forward", "backward", True))
     assert inc == ["m4_folded_dit"] and c["h_dif_t2048"]["executed"] == "fft_dif_matrix_batch"
+    c, _ = TB.candidates(TB.Shape(2048, 16, "dit"))
+    assert {k for k in c if k.startswith("hyb_")} == {"hyb_t16", "hyb_t32", "hyb_t64", "hyb_t128"}
     for shape in TB.default_shapes():
         for desc in TB.candidates(shape)[0].values():
+            if desc.get("composition"):
+                continue  # composition candidates are promoted through their own table
             e = {"N": shape.n, "batch": shape.batch, "direction": shape.direction, **desc}
             from bfft.selector import entry_contract_violations
 
@@ -126,3 +130,35 @@ def test_built_table_selects_through_the_selector():
 
     p = plan_fft("dit", 4096, batch=256, profile_hash=ph, table=t, env_hash=ENV, transform_type="r2c")
     assert not p.fallback and p.executed == "fft_dif_matrix_batch" and p.params["real_compat"]
+
+
+def _with_conf(rec, name, ms):
+    rec["confirmation"] = {name: {"p50_ms": ms, "mad_ms": 0.001, "p95_ms": ms * 1.05, "trials": 20}}
+    return rec
+
+
+def test_composition_promotion():
+    from bfft.composition import composition_select, table_violations
+
+    s1 = TB.Shape(2048, 16, "dit")
+    s2 = TB.Shape(4096, 16, "dit")
+    r1 = _with_conf(_shape_rec(s1, {"m4_spread_dit": 1.0, "m4_folded_dit": 0.9, "m2_dit_t2048": 0.2,
+                                    "hyb_t64": 0.15, "hyb_t32": 0.3}), "hyb_t64", 0.151)
+    r2 = _shape_rec(s2, {"m4_spread_dit": 1.0, "m4_folded_dit": 0.9, "m2_dit_t4096": 0.2, "hyb_t64": 0.199})
+    run = _run([r1, r2])
+    sel = TB.build_table([run])
+    assert all(e["flow_id"] != "hybrid-4step" for e in sel["entries"])  # never a selector entry
+    table, notes = TB.build_composition_table([run], sel, sources=["run.json.gz"])
+    assert table is not None and len(table["entries"]) == 1
+    e = table["entries"][0]
+    assert (e["N"], e["batch"], e["tile"], e["incumbent_flow"]) == (2048, 16, 64, "m2_dit_t2048")
+    assert abs(e["guard_pct"] - 25.0) < 1e-9 and e["evidence"]["confirmation_session"]
+    assert table_violations(table) == []
+    assert any("0.5%" in n or "not promoted" in n for n in notes)  # 4096: +0.5% < guard
+    ph = DeviceProfile.load().hash()
+    assert composition_select("dit", 2048, batch=16, profile_hash=ph, env_hash=ENV, table=table)["tile"] == 64
+    assert composition_select("dit", 2048, batch=16, profile_hash=ph, env_hash="f" * 16, table=table) is None
+    # no confirmation session -> no promotion
+    r3 = _shape_rec(s1, {"m4_spread_dit": 1.0, "m4_folded_dit": 0.9, "m2_dit_t2048": 0.2, "hyb_t64": 0.1})
+    t3, notes3 = TB.build_composition_table([_run([r3])], sel)
+    assert t3 is None and any("confirmation" in n for n in notes3)
