@@ -456,3 +456,29 @@ def test_host_buffer_execution(n, b, tt, chunks):
     dev_out = host(execute_fft_plan(p, xt.cuda()))
     assert np.array_equal(got, dev_out)
     assert rel_l2_per_transform(got.reshape(ref.shape), ref) <= TOL_F64
+
+
+def test_installed_composition_table_selects_and_executes():
+    """The promoted exact-shape 4-step entries resolve through plan_fft as
+    selection_source='composition' (run_hybrid) and execute within tolerance;
+    shapes without an entry keep the selector's plan."""
+    from bfft.composition import load_composition_table
+    from bfft.config import DeviceProfile
+    from bfft.envcheck import current_env_hash
+
+    comp = load_composition_table()
+    if comp is None:
+        pytest.skip("no composition promoted on this stack")
+    if current_env_hash() != comp["env_hash"]:
+        pytest.skip(f"composition table bound to env {comp['env_hash']}, this box is {current_env_hash()}")
+    ph = DeviceProfile.load().hash()
+    rng = np.random.default_rng(12)
+    for e in comp["entries"]:
+        n, b = e["N"], e["batch"]
+        p = bfft.plan_fft("dit", n, batch=b, profile_hash=ph)
+        assert p.selection_source == "composition" and p.executed == "run_hybrid" and p.params["tile"] == e["tile"]
+        x = cplx(rng, (b, n))
+        y = host(execute_fft_plan(p, dev(x if b > 1 else x[0]))).reshape(b, n)
+        assert rel_l2_per_transform(y, _f64(x)) <= TOL_F64, (n, b)
+    p = bfft.plan_fft("dit", 2048, batch=16, profile_hash=ph)
+    assert p.selection_source == "table"
