@@ -605,16 +605,17 @@ __global__ void __launch_bounds__(PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>::THREADS,
     const uint32_t lo_mask = (1u << lo_bits) - 1u;
     if (tws) {
         const int nlo = 1 << lo_bits, nhi = a.tw.log2n > lo_bits ? 1 << (a.tw.log2n - lo_bits) : 0;
-        for (int i = threadIdx.x; i < nlo; i += blockDim.x) tw2[i] = a.tw.lo[i];
-        for (int i = threadIdx.x; i < nhi; i += blockDim.x) tw2[nlo + i] = a.tw.hi[i];
+        for (int i = threadIdx.x; i < nlo; i += blockDim.x) tw2[i + (i >> 4)] = a.tw.lo[i];
+        for (int i = threadIdx.x; i < nhi; i += blockDim.x) tw2[nlo + (nlo >> 4) + i] = a.tw.hi[i];
         __syncthreads();
     }
-    const float2* tw2hi = tw2 + (1 << lo_bits);
+    const float2* tw2hi = tw2 + (1 << lo_bits) + ((1 << lo_bits) >> 4);
     const uint32_t nmask = a.tw.log2n >= 32 ? 0xffffffffu : (1u << a.tw.log2n) - 1u;
     auto twiddle = [&](uint32_t e) -> float2 {
         if (!tws) return tw_two_level(a.tw, e);
         e &= nmask;
-        const float2 w = tw2[e & lo_mask];
+        const uint32_t li = e & lo_mask;
+        const float2 w = tw2[li + (li >> 4)];  // lo table padded by one entry per 16: strided lanes spread over banks
         return a.tw.log2n > lo_bits ? cmul(w, tw2hi[e >> lo_bits]) : w;
     };
     const int tid = threadIdx.x;
@@ -624,6 +625,7 @@ __global__ void __launch_bounds__(PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>::THREADS,
     const int64_t imask = (int64_t(1) << a.inner_log2) - 1;
     const uint32_t in_stride = (uint32_t)a.in_stride, out_stride = (uint32_t)a.out_stride;
     const float osr = a.scale, osi = a.conj_out ? -a.scale : a.scale;
+    const bool scaled = a.scale != 1.0f || a.conj_out;  // uniform: skip the epilogue multiply when it is 1
 
     auto issue = [&](int64_t tile, float2* buf) {
         if (LMAP == 1) {
@@ -689,7 +691,7 @@ __global__ void __launch_bounds__(PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>::THREADS,
             const int k = t + m * G::TF;
             float2 val = v[m];
             if (a.tw_mode == 2) val = cmul(val, twiddle((uint32_t)k * cmul32));
-            v[m] = make_float2(val.x * osr, val.y * osi);
+            v[m] = scaled ? make_float2(val.x * osr, val.y * osi) : val;
         }
 
         if constexpr (SMAP == 0) {
@@ -745,9 +747,9 @@ static cudaError_t launch_pass_t(const float2* in, float2* out, const PassArgs& 
         const int lob = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
         const int nlo = 1 << lob, nhi = a.tw.log2n > lob ? 1 << (a.tw.log2n - lob) : 0;
         int c = 0;
-        while ((1 << c) < nlo + nhi) ++c;
+        while ((1 << c) < nlo + (nlo >> 4) + nhi) ++c;
         if (c <= kTw2MaxLog2 && G::SMEM + ((size_t)sizeof(float2) << c) <= kSmemCap) {
-            b.tw_smem_entries = nlo + nhi;
+            b.tw_smem_entries = nlo + (nlo >> 4) + nhi;
             cls = c + 1;
         }
     }

@@ -117,6 +117,10 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+__host__ __device__ constexpr uint32_t rev4(int m) {
+    return static_cast<uint32_t>(((m & 1) << 3) | ((m & 2) << 1) | ((m & 4) >> 1) | ((m & 8) >> 3));
+}
+
 // ROWS 0: outputs are columns too (one tensor store per tile);
 // ROWS 1: each sub-FFT's output is a contiguous row (one bulk copy each).
 template <int LOG2L, int ROWS>
@@ -156,6 +160,7 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
     const int64_t ntiles = a.nsub / G::K;
     const int64_t imask = (int64_t(1) << a.inner_log2) - 1;
     const float osr = a.scale, osi = a.conj_out ? -a.scale : a.scale;
+    const bool scaled = a.scale != 1.0f || a.conj_out;  // uniform: skip the epilogue multiply when it is 1
 
     fill_stockham_twiddles<LOG2L>(tw_smem);
     const bool tws = a.tw_smem_entries > 0;
@@ -163,15 +168,16 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
     const uint32_t lo_mask = (1u << lo_bits) - 1u;
     if (tws) {
         const int nlo = 1 << lo_bits, nhi = a.tw.log2n > lo_bits ? 1 << (a.tw.log2n - lo_bits) : 0;
-        for (int i = tid; i < nlo; i += blockDim.x) tw2[i] = a.tw.lo[i];
-        for (int i = tid; i < nhi; i += blockDim.x) tw2[nlo + i] = a.tw.hi[i];
+        for (int i = tid; i < nlo; i += blockDim.x) tw2[i + (i >> 4)] = a.tw.lo[i];
+        for (int i = tid; i < nhi; i += blockDim.x) tw2[nlo + (nlo >> 4) + i] = a.tw.hi[i];
     }
-    const float2* tw2hi = tw2 + (1 << lo_bits);
+    const float2* tw2hi = tw2 + (1 << lo_bits) + ((1 << lo_bits) >> 4);
     const uint32_t nmask = a.tw.log2n >= 32 ? 0xffffffffu : (1u << a.tw.log2n) - 1u;
     auto twiddle = [&](uint32_t e) -> float2 {
         if (!tws) return tw_two_level(a.tw, e);
         e &= nmask;
-        const float2 w = tw2[e & lo_mask];
+        const uint32_t li = e & lo_mask;
+        const float2 w = tw2[li + (li >> 4)];  // lo table padded by one entry per 16: strided lanes spread over banks
         return a.tw.log2n > lo_bits ? cmul(w, tw2hi[e >> lo_bits]) : w;
     };
     if (tid == 0) {
@@ -180,6 +186,10 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
         fence_proxy_async_smem();
     }
     __syncthreads();
+
+    // bit reversal over log2 L bits of e = t + m TF (t < TF, m < 16) is
+    // rev(t) * 16 + rev4(m): a per-thread base plus a constant per element
+    const uint32_t rt16 = LOG2L > 4 ? (brev_bits(static_cast<uint32_t>(t), LOG2L - 4) << 4) : 0u;
 
     auto issue = [&](int64_t tl, int s) {  // thread 0 only
         const int64_t f0 = tl * G::K;
@@ -208,7 +218,7 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
 #pragma unroll
         for (int m = 0; m < 16; ++m) {
             const uint32_t e = static_cast<uint32_t>(t + m * G::TF);
-            const uint32_t pe = a.in_elem_bitrev ? brev_bits(e, LOG2L) : e;
+            const uint32_t pe = a.in_elem_bitrev ? rt16 + rev4(m) : e;
             float2 val = ok ? buf[pe * G::K + cl] : make_float2(0.f, 0.f);
             if (a.conj_in) val.y = -val.y;
             if (a.tw_mode == 1) val = cmul(val, twiddle(e * cmul32));
@@ -227,11 +237,11 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
             const uint32_t k = static_cast<uint32_t>(t + m * G::TF);
             float2 val = v[m];
             if (a.tw_mode == 2) val = cmul(val, twiddle(k * cmul32));
-            val = make_float2(val.x * osr, val.y * osi);
+            if (scaled) val = make_float2(val.x * osr, val.y * osi);
             if constexpr (ROWS) {
                 buf[cl * (G::L + G::RPAD) + k] = val;
             } else {
-                const uint32_t pk = a.out_elem_bitrev ? brev_bits(k, LOG2L) : k;
+                const uint32_t pk = a.out_elem_bitrev ? rt16 + rev4(m) : k;
                 buf[pk * G::K + cl] = val;
             }
         }
@@ -300,6 +310,7 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
     const int64_t ntiles = (a.nsub + G::K - 1) / G::K;
     const int64_t imask = (int64_t(1) << a.inner_log2) - 1;
     const float osr = a.scale, osi = a.conj_out ? -a.scale : a.scale;
+    const bool scaled = a.scale != 1.0f || a.conj_out;  // uniform: skip the epilogue multiply when it is 1
     const int NST = out_contig ? 1 : G::K;  // threads that issue (and wait for) stores
 
     fill_stockham_twiddles<LOG2L>(tw_smem);
@@ -308,15 +319,16 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
     const uint32_t lo_mask = (1u << lo_bits) - 1u;
     if (tws) {
         const int nlo = 1 << lo_bits, nhi = a.tw.log2n > lo_bits ? 1 << (a.tw.log2n - lo_bits) : 0;
-        for (int i = tid; i < nlo; i += blockDim.x) tw2[i] = a.tw.lo[i];
-        for (int i = tid; i < nhi; i += blockDim.x) tw2[nlo + i] = a.tw.hi[i];
+        for (int i = tid; i < nlo; i += blockDim.x) tw2[i + (i >> 4)] = a.tw.lo[i];
+        for (int i = tid; i < nhi; i += blockDim.x) tw2[nlo + (nlo >> 4) + i] = a.tw.hi[i];
     }
-    const float2* tw2hi = tw2 + (1 << lo_bits);
+    const float2* tw2hi = tw2 + (1 << lo_bits) + ((1 << lo_bits) >> 4);
     const uint32_t nmask = a.tw.log2n >= 32 ? 0xffffffffu : (1u << a.tw.log2n) - 1u;
     auto twiddle = [&](uint32_t e) -> float2 {
         if (!tws) return tw_two_level(a.tw, e);
         e &= nmask;
-        const float2 w = tw2[e & lo_mask];
+        const uint32_t li = e & lo_mask;
+        const float2 w = tw2[li + (li >> 4)];  // lo table padded by one entry per 16: strided lanes spread over banks
         return a.tw.log2n > lo_bits ? cmul(w, tw2hi[e >> lo_bits]) : w;
     };
     auto row_in = [&](int64_t f) -> const float2* {
@@ -385,7 +397,7 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
             const uint32_t k = static_cast<uint32_t>(t + m * G::TF);
             float2 val = v[m];
             if (a.tw_mode == 2) val = cmul(val, twiddle(k * cmul32));
-            buf[cl * G::L + k] = make_float2(val.x * osr, val.y * osi);
+            buf[cl * G::L + k] = scaled ? make_float2(val.x * osr, val.y * osi) : val;
         }
         fence_proxy_async_smem();
         __syncthreads();
@@ -468,9 +480,9 @@ static cudaError_t launch_pass_tma_t(const float2* in, float2* out, const PassAr
         const int lob = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
         const int nlo = 1 << lob, nhi = a.tw.log2n > lob ? 1 << (a.tw.log2n - lob) : 0;
         int c = 0;
-        while ((1 << c) < nlo + nhi) ++c;
+        while ((1 << c) < nlo + (nlo >> 4) + nhi) ++c;
         if (c <= kTw2MaxLog2 && G::SMEM + ((size_t)sizeof(float2) << c) <= kSmemCap) {
-            b.tw_smem_entries = nlo + nhi;
+            b.tw_smem_entries = nlo + (nlo >> 4) + nhi;
             cls = c + 1;
         }
     }
@@ -515,9 +527,9 @@ static cudaError_t launch_pass_tma_rows_t(const float2* in, float2* out, const P
         const int lob = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
         const int nlo = 1 << lob, nhi = a.tw.log2n > lob ? 1 << (a.tw.log2n - lob) : 0;
         int c = 0;
-        while ((1 << c) < nlo + nhi) ++c;
+        while ((1 << c) < nlo + (nlo >> 4) + nhi) ++c;
         if (c <= kTw2MaxLog2 && G::SMEM + ((size_t)sizeof(float2) << c) <= kSmemCap) {
-            b.tw_smem_entries = nlo + nhi;
+            b.tw_smem_entries = nlo + (nlo >> 4) + nhi;
             cls = c + 1;
         }
     }
