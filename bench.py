@@ -477,10 +477,12 @@ def run_4step(args, wl, ctx) -> dict:
         desc = {"plan": plan.executed, "plan_params": plan.params, "plan_source": plan_src,
                 "parallelism": "1 GPU"}
     else:
-        f = bdist.DistributedFFT(n, device=ctx.dev)
+        f = bdist.DistributedFFT(n, device=ctx.dev, exchange=args.exchange)
         fn = f.execute
-        desc = {"plan": "DistributedFFT (4-step, NCCL all_to_all_single x3)", "factors": [f.n1, f.n2],
-                "parallelism": f"slab x{ctx.world}, 3 all-to-alls per transform"}
+        how = ("transposes fused with the exchanges: peer stores over NVLink into the other ranks' buffers "
+               "(CUDA IPC), stream-ordered barriers" if f.exchange == "p2p" else "NCCL all_to_all_single x3")
+        desc = {"plan": f"DistributedFFT (4-step, {how})", "exchange": f.exchange, "factors": [f.n1, f.n2],
+                "parallelism": f"slab x{ctx.world}, 3 exchanges per transform"}
     for _ in range(args.warmup):
         y = fn(x)
     del y
@@ -500,7 +502,7 @@ def run_4step(args, wl, ctx) -> dict:
         # of the rank's slab over NVLink
         wire = 3.0 * 8.0 * slab * (ctx.world - 1) / ctx.world
         nvl = wire / (ms_step / 1e3) / 1e9
-        roofline = {"bound": "hbm", "kernel": "whole step (transposes, row passes, NCCL all-to-alls)",
+        roofline = {"bound": "hbm", "kernel": "whole step (transposes with exchanges, row passes)",
                     "achieved": 16.0 * slab / (ms_step / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                     "peak_source": peak_src, "traffic": None,
                     "nvlink": {"bytes_per_step_per_gpu": wire, "achieved_gbs_per_direction": nvl,
@@ -534,6 +536,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="5a")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", choices=("p2p", "nccl"), default=None,
+                    help="5b on 2+ GPUs: fused peer-store exchanges (default) or NCCL all-to-alls")
     ap.add_argument("--n", type=int, default=None,
                     help="sweep workload: transform length N (power of two <= 2^24), batch 2^24 / N")
     ap.add_argument("--batch", type=int, default=None,

@@ -217,6 +217,26 @@ BFFT_EXPORT bfft_status bfft_dist_plan_create(int64_t n1, int64_t n2, int32_t nr
 BFFT_EXPORT bfft_status bfft_dist_workspace_size(bfft_dist_plan_t plan, size_t* bytes);
 BFFT_EXPORT bfft_status bfft_dist_phase(bfft_dist_plan_t plan, int32_t phase, const void* in, void* out,
                                         void* workspace, size_t workspace_bytes, void* stream);
+/* Peer-to-peer mode of the same transform: every exchange is fused into the
+ * transpose before it.  Each rank owns two exchange buffers (2 N/P complex64,
+ * allocated by bfft_dist_p2p_prepare); once every rank's buffers are mapped
+ * into every process (bfft_dist_p2p_attach with the nranks CUDA IPC handles
+ * of prepare, in rank order -- or bfft_dist_p2p_attach_pointers with device
+ * pointers when all ranks live in one process), phase k writes its result
+ * over NVLink straight into the destination ranks' buffers, in the layout
+ * their next phase reads:
+ *     barrier -> phase 0 -> barrier -> phase 1 -> barrier -> phase 2 -> barrier -> phase 3
+ * where a barrier means every rank's previous phase has completed (the host
+ * orders it, e.g. a stream-ordered all-reduce of one word).  Phase 0 reads
+ * `in` (the rank's slab), phase 3 writes `out` (the rank's output slab);
+ * phases 1 and 2 need bfft_dist_workspace_size bytes of workspace.  No
+ * device-side waits, no multicast: plain stores to peer memory. */
+BFFT_EXPORT bfft_status bfft_dist_p2p_prepare(bfft_dist_plan_t plan, void* exchange_base, void* ipc_handle,
+                                              size_t* handle_bytes);
+BFFT_EXPORT bfft_status bfft_dist_p2p_attach(bfft_dist_plan_t plan, const void* handles);
+BFFT_EXPORT bfft_status bfft_dist_p2p_attach_pointers(bfft_dist_plan_t plan, void* const* exchange_bases);
+BFFT_EXPORT bfft_status bfft_dist_p2p_phase(bfft_dist_plan_t plan, int32_t phase, const void* in, void* out,
+                                            void* workspace, size_t workspace_bytes, void* stream);
 /* Kernel launches one bfft_dist_phase call of `phase` enqueues. */
 BFFT_EXPORT bfft_status bfft_dist_plan_launches(bfft_dist_plan_t plan, int32_t phase, int* launches);
 BFFT_EXPORT bfft_status bfft_dist_plan_destroy(bfft_dist_plan_t plan);

@@ -32,7 +32,8 @@ EXPORTS = ("bfft_api_version", "bfft_last_error", "bfft_plan_create", "bfft_plan
            "bfft_index_map", "bfft_launch_counter", "bfft_hybrid_c2c_noalloc",
            "bfft_dist_batch_shard", "bfft_dist_plan_create", "bfft_dist_workspace_size",
            "bfft_dist_phase", "bfft_dist_plan_launches", "bfft_dist_plan_destroy", "bfft_device_status",
-           "bfft_stream_plan_create", "bfft_stream_plan_info", "bfft_stream_execute", "bfft_stream_plan_destroy")
+           "bfft_stream_plan_create", "bfft_stream_plan_info", "bfft_stream_execute", "bfft_stream_plan_destroy",
+           "bfft_dist_p2p_prepare", "bfft_dist_p2p_attach", "bfft_dist_p2p_attach_pointers", "bfft_dist_p2p_phase")
 
 
 class PlanDesc(ctypes.Structure):
@@ -95,6 +96,10 @@ def load() -> ctypes.CDLL:
         L.bfft_stream_plan_info.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz), ctypes.POINTER(ctypes.c_int)]
         L.bfft_stream_execute.argtypes = [vp, vp, vp, vp]
         L.bfft_stream_plan_destroy.argtypes = [vp]
+        L.bfft_dist_p2p_prepare.argtypes = [vp, ctypes.POINTER(vp), ctypes.c_char_p, ctypes.POINTER(sz)]
+        L.bfft_dist_p2p_attach.argtypes = [vp, ctypes.c_char_p]
+        L.bfft_dist_p2p_attach_pointers.argtypes = [vp, ctypes.POINTER(vp)]
+        L.bfft_dist_p2p_phase.argtypes = [vp, i32, vp, vp, vp, sz, vp]
         for name in EXPORTS:
             fn = getattr(L, name)
             if name not in ("bfft_api_version", "bfft_last_error", "bfft_launch_counter"):
@@ -194,6 +199,27 @@ class NativeDistPlan:
     def phase(self, phase: int, in_ptr: int, out_ptr: int, ws_ptr: int, ws_bytes: int, stream: int) -> None:
         check(load().bfft_dist_phase(self.handle, int(phase), in_ptr, out_ptr, ws_ptr, ws_bytes, stream),
               "bfft_dist_phase")
+
+    # ---- peer-to-peer mode ----
+    def p2p_prepare(self) -> tuple[int, bytes]:
+        """(device address of this rank's exchange buffers, its CUDA IPC handle)."""
+        base, n = ctypes.c_void_p(), ctypes.c_size_t()
+        check(load().bfft_dist_p2p_prepare(self.handle, ctypes.byref(base), None, ctypes.byref(n)),
+              "bfft_dist_p2p_prepare")
+        buf = ctypes.create_string_buffer(int(n.value))
+        check(load().bfft_dist_p2p_prepare(self.handle, None, buf, ctypes.byref(n)), "bfft_dist_p2p_prepare")
+        return int(base.value), buf.raw
+
+    def p2p_attach(self, handles: bytes) -> None:
+        check(load().bfft_dist_p2p_attach(self.handle, handles), "bfft_dist_p2p_attach")
+
+    def p2p_attach_pointers(self, bases: list[int]) -> None:
+        arr = (ctypes.c_void_p * len(bases))(*bases)
+        check(load().bfft_dist_p2p_attach_pointers(self.handle, arr), "bfft_dist_p2p_attach_pointers")
+
+    def p2p_phase(self, phase: int, in_ptr: int, out_ptr: int, ws_ptr: int, ws_bytes: int, stream: int) -> None:
+        check(load().bfft_dist_p2p_phase(self.handle, int(phase), in_ptr, out_ptr, ws_ptr, ws_bytes, stream),
+              "bfft_dist_p2p_phase")
 
 
 def _destroy_stream(handle: int) -> None:

@@ -78,6 +78,31 @@ class _NativePhases:
         self.plan.phase(k, x.data_ptr(), out.data_ptr(), self.ws.data_ptr(), self.ws.numel(), stream)
 
 
+class _NativeP2PPhases(_NativePhases):
+    """Device phases with every exchange fused into the transpose before it:
+    results are stored over NVLink straight into the destination ranks'
+    exchange buffers (CUDA IPC mappings, plain peer stores, no multicast)."""
+
+    p2p = True
+
+    def __init__(self, n1, n2, world, rank, transform_direction, norm, device, row_tiles, group):
+        super().__init__(n1, n2, world, rank, transform_direction, norm, device, row_tiles)
+        base, handle = self.plan.p2p_prepare()
+        if world > 1:
+            mine = torch.tensor(list(handle), dtype=torch.uint8, device=device)
+            every = torch.empty(world * len(handle), dtype=torch.uint8, device=device)
+            dist.all_gather_into_tensor(every, mine, group=group)
+            self.plan.p2p_attach(bytes(every.cpu().tolist()))
+        else:
+            self.plan.p2p_attach_pointers([base])
+        self.launches = sum(self.plan.launches) - 2 * (1 if world > 1 else 0) - 1  # no chunk permutes
+
+    def phase(self, k: int, x, out) -> None:
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        self.plan.p2p_phase(k, x.data_ptr() if x is not None else 0, out.data_ptr() if out is not None else 0,
+                            self.ws.data_ptr(), self.ws.numel(), stream)
+
+
 class DistributedFFT:
     """One C2C transform of ``n`` points over the ranks of ``group``.
 
@@ -88,7 +113,8 @@ class DistributedFFT:
     power of two dividing both factors of ``n = n1 * n2``."""
 
     def __init__(self, n: int, *, n1: int | None = None, group=None, transform_direction: str = "forward",
-                 norm: str = "backward", device=None, row_tiles: tuple[int, int] = (0, 0), phases=None):
+                 norm: str = "backward", device=None, row_tiles: tuple[int, int] = (0, 0), phases=None,
+                 exchange: str | None = None):
         if transform_direction not in ("forward", "inverse"):
             raise ValueError(f"transform_direction must be 'forward' or 'inverse', got {transform_direction!r}")
         if norm not in ("none", "forward", "backward", "ortho"):
@@ -105,11 +131,21 @@ class DistributedFFT:
         self.n, self.n1, self.n2, self.group = n, n1, n2, group
         self.slab = n // self.world
         self.transform_direction, self.norm = transform_direction, norm
+        if exchange is None:
+            exchange = "p2p" if self.world > 1 else "nccl"
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange must be 'p2p' or 'nccl', got {exchange!r}")
         if phases is None:
             dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-            phases = _NativePhases(n1, n2, self.world, self.rank, transform_direction, norm, dev, row_tiles)
+            if exchange == "p2p":
+                phases = _NativeP2PPhases(n1, n2, self.world, self.rank, transform_direction, norm, dev, row_tiles,
+                                          group)
+            else:
+                phases = _NativePhases(n1, n2, self.world, self.rank, transform_direction, norm, dev, row_tiles)
+        self.exchange = "p2p" if getattr(phases, "p2p", False) else "nccl"
         self.phases = phases
         self._bufs = None
+        self._flag = None
 
     @property
     def launches(self) -> int:
@@ -120,6 +156,15 @@ class DistributedFFT:
         if self._bufs is None:
             self._bufs = (self.phases.empty(self.slab), self.phases.empty(self.slab))
         return self._bufs
+
+    def _barrier(self) -> None:
+        """Stream-ordered: work after it starts once every rank's work before it
+        has completed (an all-reduce of one word)."""
+        if self.world == 1:
+            return
+        if self._flag is None:
+            self._flag = torch.zeros(1, dtype=torch.int32, device=self.phases.device)
+        dist.all_reduce(self._flag, group=self.group)
 
     def _exchange(self, send: torch.Tensor, recv: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
@@ -134,9 +179,20 @@ class DistributedFFT:
             raise TypeError(f"x must be complex64, got {x.dtype}")
         if x.dim() != 1 or x.numel() != self.slab or not x.is_contiguous():
             raise ValueError(f"x must be a contiguous 1-D slab of {self.slab} points, got {tuple(x.shape)}")
-        a, b = self._buffers()
         if out is None:
             out = self.phases.empty(self.slab)
+        if self.exchange == "p2p":
+            # every phase writes into the other ranks' buffers: all ranks must
+            # have finished the previous phase (and the previous execution)
+            self._barrier()
+            self.phases.phase(0, x, None)
+            for k in (1, 2):
+                self._barrier()
+                self.phases.phase(k, None, None)
+            self._barrier()
+            self.phases.phase(3, None, out)
+            return out
+        a, b = self._buffers()
         self.phases.phase(0, x, a)
         cur = self._exchange(a, b)
         for k in (1, 2):

@@ -24,10 +24,12 @@
 // between these calls (bfft/dist.py); every phase only touches this rank's
 // device memory.
 #include <cmath>
+#include <cstring>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdint>
 #include <string>
+#include <vector>
 
 #include "../../include/bfft.h"
 #include "bfft_kernels.cuh"
@@ -90,6 +92,45 @@ __global__ void __launch_bounds__(256) k_chunk_permute(const V* __restrict__ in,
     }
 }
 
+// Transpose fused with the exchange: element (r, c) of the local rows x cols
+// matrix goes to rank d = c >> log2_dc, at offset
+// (c & (dc - 1)) * dst_ld + dst_off + r of that rank's exchange buffer
+// (peers[d], mapped into this process), optionally times W_N^{(row0 + r) c},
+// conjugated and scaled.  Writes are runs of 32 consecutive r (256 bytes)
+// over NVLink; every thread fences at system scope after its stores so the
+// host-ordered barrier that follows publishes them.
+__global__ void __launch_bounds__(256) k_scatter_transpose(const float2* __restrict__ in, float2* const* peers,
+                                                           int64_t rows, int64_t cols, int64_t tiles_c,
+                                                           int log2_dc, int64_t dst_ld, int64_t dst_off, TwoLevel tw,
+                                                           int use_tw, uint32_t row0, int conj, float scale) {
+    __shared__ float2 t[kTT][kTT + 1];
+    const int64_t tile = blockIdx.x;
+    const int64_t r0 = (tile / tiles_c) * kTT, c0 = (tile % tiles_c) * kTT;
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    const int64_t dmask = ((int64_t)1 << log2_dc) - 1;
+#pragma unroll
+    for (int j = ty; j < kTT; j += 8) {
+        const int64_t r = r0 + j, c = c0 + tx;
+        if (r < rows && c < cols) {
+            float2 v = in[r * cols + c];
+            if (conj) v.y = -v.y;
+            if (use_tw) v = cmul(v, tw_two_level(tw, (row0 + (uint32_t)r) * (uint32_t)c));
+            t[j][tx] = v;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = ty; j < kTT; j += 8) {
+        const int64_t c = c0 + j, r = r0 + tx;
+        if (r < rows && c < cols) {
+            const float2 v = t[tx][j];
+            float2* dst = peers[c >> log2_dc];
+            dst[(c & dmask) * dst_ld + dst_off + r] = make_float2(v.x * scale, v.y * scale);
+        }
+    }
+    __threadfence_system();
+}
+
 int g_sms = 0;
 
 cudaError_t launch_transpose(const float2* in, float2* out, int64_t rows, int64_t cols, const TwoLevel& tw,
@@ -104,6 +145,16 @@ int ilog2(int64_t v) {
     int b = 0;
     while (((int64_t)1 << b) < v) ++b;
     return b;
+}
+
+cudaError_t launch_scatter(const float2* in, float2* const* peers, int64_t rows, int64_t cols, int64_t dc,
+                           int64_t dst_ld, int64_t dst_off, const TwoLevel& tw, int use_tw, uint32_t row0, int conj,
+                           float scale, cudaStream_t s) {
+    const int64_t tr = (rows + kTT - 1) / kTT, tc = (cols + kTT - 1) / kTT;
+    k_scatter_transpose<<<(unsigned)(tr * tc), dim3(kTT, 8), 0, s>>>(in, peers, rows, cols, tc, ilog2(dc), dst_ld,
+                                                                     dst_off, tw, use_tw, row0, conj, scale);
+    count_launches(1);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_chunk_permute(const float2* in, float2* out, int64_t A, int64_t B, int64_t C, int conj,
@@ -172,6 +223,13 @@ struct bfft_dist_plan_s {
     bfft_plan_t row1 = nullptr, row2 = nullptr;
     size_t row_ws = 0;
     float scale = 1.0f;
+    // peer-to-peer mode: this rank's two exchange buffers (X1 [M2][N1] and
+    // X2 [M1][N2]), every rank's buffers as mapped here, and the device tables
+    float2* xbuf = nullptr;
+    std::vector<void*> opened;     // peer allocations opened through CUDA IPC (closed on destroy)
+    float2** d_peers_x1 = nullptr;  // nranks entries
+    float2** d_peers_x2 = nullptr;
+    bool attached = false;
 };
 
 namespace {
@@ -378,7 +436,132 @@ bfft_status bfft_dist_plan_destroy(bfft_dist_plan_t plan) {
     if (plan->row1) bfft_plan_destroy(plan->row1);
     if (plan->row2) bfft_plan_destroy(plan->row2);
     if (plan->twmem) cudaFree(plan->twmem);
+    for (void* ptr : plan->opened) cudaIpcCloseMemHandle(ptr);
+    if (plan->d_peers_x1) cudaFree(plan->d_peers_x1);
+    if (plan->d_peers_x2) cudaFree(plan->d_peers_x2);
+    if (plan->xbuf) cudaFree(plan->xbuf);
     delete plan;
+    return BFFT_OK;
+}
+
+static bfft_status p2p_attach_bases(bfft_dist_plan_t plan, void* const* bases) {
+    const size_t slab = (size_t)(plan->n / plan->nranks);
+    std::vector<float2*> x1(plan->nranks), x2(plan->nranks);
+    for (int p = 0; p < plan->nranks; ++p) {
+        if (!bases[p]) return dfail(BFFT_ERR_VALUE, "NULL exchange buffer for rank %d", p);
+        x1[p] = static_cast<float2*>(bases[p]);
+        x2[p] = x1[p] + slab;
+    }
+    const size_t tb = sizeof(float2*) * (size_t)plan->nranks;
+    cudaError_t e = cudaSuccess;
+    if (!plan->d_peers_x1) e = cudaMalloc(&plan->d_peers_x1, tb);
+    if (e == cudaSuccess && !plan->d_peers_x2) e = cudaMalloc(&plan->d_peers_x2, tb);
+    if (e == cudaSuccess) e = cudaMemcpy(plan->d_peers_x1, x1.data(), tb, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(plan->d_peers_x2, x2.data(), tb, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return dcuda(e, "peer tables");
+    plan->attached = true;
+    return BFFT_OK;
+}
+
+bfft_status bfft_dist_p2p_prepare(bfft_dist_plan_t plan, void* exchange_base, void* ipc_handle,
+                                  size_t* handle_bytes) {
+    if (!plan) return dfail(BFFT_ERR_VALUE, "NULL plan");
+    if (handle_bytes) *handle_bytes = sizeof(cudaIpcMemHandle_t);
+    DevGuard g(plan->device);
+    if (!g.ok) return dfail(BFFT_ERR_CUDA, "cannot select device %d", plan->device);
+    if (!plan->xbuf) {
+        cudaError_t e = cudaMalloc(&plan->xbuf, sizeof(float2) * 2 * (size_t)(plan->n / plan->nranks));
+        if (e != cudaSuccess)
+            return e == cudaErrorMemoryAllocation ? dfail(BFFT_ERR_ALLOC, "exchange buffers: out of device memory")
+                                                  : dcuda(e, "exchange buffers");
+    }
+    if (exchange_base) *(void**)exchange_base = plan->xbuf;
+    if (ipc_handle) {
+        cudaIpcMemHandle_t h;
+        cudaError_t e = cudaIpcGetMemHandle(&h, plan->xbuf);
+        if (e != cudaSuccess) return dcuda(e, "cudaIpcGetMemHandle");
+        memcpy(ipc_handle, &h, sizeof h);
+    }
+    return BFFT_OK;
+}
+
+bfft_status bfft_dist_p2p_attach(bfft_dist_plan_t plan, const void* handles) {
+    if (!plan || !handles) return dfail(BFFT_ERR_VALUE, "NULL plan or handles");
+    if (!plan->xbuf) return dfail(BFFT_ERR_VALUE, "bfft_dist_p2p_prepare first");
+    DevGuard g(plan->device);
+    if (!g.ok) return dfail(BFFT_ERR_CUDA, "cannot select device %d", plan->device);
+    std::vector<void*> bases(plan->nranks, nullptr);
+    const char* hb = static_cast<const char*>(handles);
+    for (int p = 0; p < plan->nranks; ++p) {
+        if (p == plan->rank) {
+            bases[p] = plan->xbuf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hb + (size_t)p * sizeof h, sizeof h);
+        void* ptr = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return dcuda(e, "cudaIpcOpenMemHandle");
+        plan->opened.push_back(ptr);
+        bases[p] = ptr;
+    }
+    return p2p_attach_bases(plan, bases.data());
+}
+
+bfft_status bfft_dist_p2p_attach_pointers(bfft_dist_plan_t plan, void* const* exchange_bases) {
+    if (!plan || !exchange_bases) return dfail(BFFT_ERR_VALUE, "NULL plan or pointer table");
+    DevGuard g(plan->device);
+    if (!g.ok) return dfail(BFFT_ERR_CUDA, "cannot select device %d", plan->device);
+    return p2p_attach_bases(plan, exchange_bases);
+}
+
+bfft_status bfft_dist_p2p_phase(bfft_dist_plan_t plan, int32_t phase, const void* in, void* out, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+    if (!plan) return dfail(BFFT_ERR_VALUE, "NULL plan");
+    if (!plan->attached) return dfail(BFFT_ERR_VALUE, "peer-to-peer phases need bfft_dist_p2p_attach first");
+    if (phase < 0 || phase > 3) return dfail(BFFT_ERR_VALUE, "phase must be 0..3, got %d", phase);
+    if ((phase == 0 && !in) || (phase == 3 && !out)) return dfail(BFFT_ERR_VALUE, "NULL data pointer");
+    if (((uintptr_t)in | (uintptr_t)out | (uintptr_t)workspace) & 15)
+        return dfail(BFFT_ERR_VALUE, "buffers must be 16-byte aligned");
+    size_t need = 0;
+    bfft_dist_workspace_size(plan, &need);
+    if ((phase == 1 || phase == 2) && (!workspace || workspace_bytes < need))
+        return dfail(BFFT_ERR_WORKSPACE, "phase %d needs %zu workspace bytes, got %zu", phase, need,
+                     workspace ? workspace_bytes : (size_t)0);
+    DevGuard g(plan->device);
+    if (!g.ok) return dfail(BFFT_ERR_CUDA, "cannot select device %d", plan->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    const int64_t P = plan->nranks, m1 = plan->m1, m2 = plan->m2, n1 = plan->n1, n2 = plan->n2, r = plan->rank;
+    const int inv = plan->tdir == BFFT_INVERSE;
+    const size_t slab = (size_t)(plan->n / P);
+    float2* x1 = plan->xbuf;  // [M2][N1]: exchange 1 (and 3) lands here
+    float2* x2 = plan->xbuf + slab;  // [M1][N2]: exchange 2
+    float2* tmp = (float2*)workspace;
+    void* row_ws = workspace ? (char*)workspace + sizeof(float2) * slab : nullptr;
+    const size_t row_ws_bytes = workspace_bytes > sizeof(float2) * slab ? workspace_bytes - sizeof(float2) * slab : 0;
+    cudaError_t e = cudaSuccess;
+    bfft_status st = BFFT_OK;
+    switch (phase) {
+        case 0:  // x_r[i][n2] -> rank n2 / M2: X1[n2 % M2][r M1 + i]
+            e = launch_scatter((const float2*)in, plan->d_peers_x1, m1, n2, m2, n1, r * m1, plan->tw, 0, 0, inv, 1.0f, s);
+            break;
+        case 1:  // rows of X1 -> [n2'][k1] -> rank k1 / M1: X2[k1 % M1][r M2 + n2'] x W_N^{n2 k1}
+            st = bfft_execute(plan->row1, x1, tmp, row_ws, row_ws_bytes, stream);
+            if (st == BFFT_OK)
+                e = launch_scatter(tmp, plan->d_peers_x2, m2, n1, m1, n2, r * m2, plan->tw, 1, (uint32_t)(r * m2), 0,
+                                   1.0f, s);
+            break;
+        case 2:  // rows of X2 -> [k1'][k2] -> rank k2 / M2: X1[k2 % M2][r M1 + k1'], conj / norm
+            st = bfft_execute(plan->row2, x2, tmp, row_ws, row_ws_bytes, stream);
+            if (st == BFFT_OK)
+                e = launch_scatter(tmp, plan->d_peers_x1, m1, n2, m2, n1, r * m1, plan->tw, 0, 0, inv, plan->scale, s);
+            break;
+        case 3:  // X1 holds X[k2 N1 + k1] for k2 in this rank's slab
+            e = cudaMemcpyAsync(out, x1, sizeof(float2) * slab, cudaMemcpyDeviceToDevice, s);
+            break;
+    }
+    if (st != BFFT_OK) return st;
+    if (e != cudaSuccess) return dcuda(e, "peer-to-peer phase");
     return BFFT_OK;
 }
 

@@ -106,6 +106,43 @@ def test_distributed_fft_single_rank_and_row_tiles():
         assert rel_l2_per_transform(y.cpu().numpy(), ref) <= TOL_F64, tiles
 
 
+@pytest.mark.parametrize("n1, n2, p, tdir, norm", [(1024, 1024, 2, "forward", "backward"),
+                                                   (256, 4096, 4, "inverse", "backward"),
+                                                   (4096, 512, 8, "forward", "ortho"), (512, 512, 1, "forward", "none")])
+def test_p2p_phases_emulated_ranks(n1, n2, p, tdir, norm):
+    """Peer-to-peer mode: the exchanges fused into the transposes (stores into
+    the other ranks' buffers); all ranks in one process on one GPU, attached
+    through device pointers, phases run rank after rank (a barrier between)."""
+    rng = np.random.default_rng(n1 * 3 + n2 + p)
+    n = n1 * n2
+    x = cplx(rng, n)
+    plans = [_lib.NativeDistPlan(n1, n2, p, r, transform_direction=tdir, norm=norm, device=0) for r in range(p)]
+    bases = [pl.p2p_prepare()[0] for pl in plans]
+    for pl in plans:
+        pl.p2p_attach_pointers(bases)
+    ws = [torch.empty(pl.workspace_bytes, dtype=torch.uint8, device=DEV) for pl in plans]
+    st = torch.cuda.current_stream().cuda_stream
+    slab = n // p
+    xs = [torch.from_numpy(x[r * slab:(r + 1) * slab].copy()).to(DEV) for r in range(p)]
+    outs = [torch.empty(slab, dtype=torch.complex64, device=DEV) for _ in range(p)]
+    before = _lib.launch_counter()
+    for k in range(4):
+        for r in range(p):
+            pl = plans[r]
+            pl.p2p_phase(k, xs[r].data_ptr() if k == 0 else 0, outs[r].data_ptr() if k == 3 else 0,
+                         ws[r].data_ptr(), ws[r].numel(), st)
+    y = torch.cat(outs).cpu().numpy()
+    assert _lib.launch_counter() > before
+    xd = x.astype(np.complex128)
+    if tdir == "forward":
+        ref = np.fft.fft(xd, norm=norm if norm != "none" else "backward")
+    else:
+        ref = np.fft.ifft(xd, norm=norm if norm != "none" else "forward")
+    assert rel_l2_per_transform(y, ref) <= TOL_F64, (n1, n2, p)
+    with pytest.raises(ValueError):  # phases before attach are refused
+        _lib.NativeDistPlan(n1, n2, p, 0).p2p_phase(1, 0, 0, ws[0].data_ptr(), ws[0].numel(), st)
+
+
 def test_dist_errors_before_launch():
     with pytest.raises(ValueError):
         _lib.NativeDistPlan(1024, 1024, 3, 0)
@@ -141,11 +178,15 @@ def _nccl_rank(rank, world, port, results):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=datetime.timedelta(seconds=120))
     try:
-        for idx, (n, tdir, norm) in enumerate([(1 << 22, "forward", "backward"), (1 << 24, "inverse", "ortho")]):
-            rng = np.random.default_rng(idx)
+        cases = [(1 << 22, "forward", "backward", "p2p"), (1 << 24, "inverse", "ortho", "p2p"),
+                 (1 << 22, "forward", "backward", "nccl"), (1 << 24, "inverse", "ortho", "nccl")]
+        for idx, (n, tdir, norm, mode) in enumerate(cases):
+            rng = np.random.default_rng(idx % 2)
             x = cplx(rng, n)
             slab = n // world
-            f = bdist.DistributedFFT(n, transform_direction=tdir, norm=norm, device=dev)
+            f = bdist.DistributedFFT(n, transform_direction=tdir, norm=norm, device=dev, exchange=mode)
+            assert f.exchange == mode
+            f.execute(torch.from_numpy(x[rank * slab:(rank + 1) * slab].copy()).to(dev))  # twice: buffer reuse
             y = f.execute(torch.from_numpy(x[rank * slab:(rank + 1) * slab].copy()).to(dev)).cpu().numpy()
             xd = x.astype(np.complex128)
             ref = np.fft.fft(xd, norm=norm) if tdir == "forward" else np.fft.ifft(xd, norm=norm)
@@ -170,7 +211,7 @@ def test_distributed_fft_over_nccl():
                            start_method="spawn")
         res = dict(results)
     for r in range(world):
-        for idx in range(2):
+        for idx in range(4):
             assert res[(r, idx)] <= TOL_F64, (r, idx, res[(r, idx)])
     shards = sorted(res[(r, "shard")] for r in range(world))
     assert shards[0][0] == 0 and sum(c for _, c in shards) == 8192
