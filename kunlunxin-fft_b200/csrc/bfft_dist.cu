@@ -96,36 +96,44 @@ __global__ void __launch_bounds__(256) k_chunk_permute(const V* __restrict__ in,
 // matrix goes to rank d = c >> log2_dc, at offset
 // (c & (dc - 1)) * dst_ld + dst_off + r of that rank's exchange buffer
 // (peers[d], mapped into this process), optionally times W_N^{(row0 + r) c},
-// conjugated and scaled.  Writes are runs of 32 consecutive r (256 bytes)
-// over NVLink; every thread fences at system scope after its stores so the
-// host-ordered barrier that follows publishes them.
+// conjugated and scaled.  A 64 x 32 tile is read row-wise (256-byte runs),
+// held transposed in shared memory, and written as 16-byte stores, 512-byte
+// runs of consecutive r per warp, over NVLink (remote ranks) or locally;
+// every thread fences at system scope after its stores so the host-ordered
+// barrier that follows publishes them.
+constexpr int kSR = 64, kSC = 32;  // scatter tile: rows x cols
 __global__ void __launch_bounds__(256) k_scatter_transpose(const float2* __restrict__ in, float2* const* peers,
                                                            int64_t rows, int64_t cols, int64_t tiles_c,
                                                            int log2_dc, int64_t dst_ld, int64_t dst_off, TwoLevel tw,
                                                            int use_tw, uint32_t row0, int conj, float scale) {
-    __shared__ float2 t[kTT][kTT + 1];
+    __shared__ __align__(16) float2 t[kSC][kSR + 2];  // [col][row], rows 16-byte aligned
     const int64_t tile = blockIdx.x;
-    const int64_t r0 = (tile / tiles_c) * kTT, c0 = (tile % tiles_c) * kTT;
-    const int tx = threadIdx.x, ty = threadIdx.y;
+    const int64_t r0 = (tile / tiles_c) * kSR, c0 = (tile % tiles_c) * kSC;
+    const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
     const int64_t dmask = ((int64_t)1 << log2_dc) - 1;
 #pragma unroll
-    for (int j = ty; j < kTT; j += 8) {
-        const int64_t r = r0 + j, c = c0 + tx;
+    for (int j = 0; j < kSR / 8; ++j) {
+        const int rl = ty + 8 * j;
+        const int64_t r = r0 + rl, c = c0 + tx;
         if (r < rows && c < cols) {
             float2 v = in[r * cols + c];
             if (conj) v.y = -v.y;
             if (use_tw) v = cmul(v, tw_two_level(tw, (row0 + (uint32_t)r) * (uint32_t)c));
-            t[j][tx] = v;
+            t[tx][rl] = make_float2(v.x * scale, v.y * scale);
         }
     }
     __syncthreads();
 #pragma unroll
-    for (int j = ty; j < kTT; j += 8) {
-        const int64_t c = c0 + j, r = r0 + tx;
-        if (r < rows && c < cols) {
-            const float2 v = t[tx][j];
-            float2* dst = peers[c >> log2_dc];
-            dst[(c & dmask) * dst_ld + dst_off + r] = make_float2(v.x * scale, v.y * scale);
+    for (int j = 0; j < kSC / 8; ++j) {
+        const int cl = ty + 8 * j;
+        const int64_t c = c0 + cl, r = r0 + 2 * tx;
+        if (c >= cols || r >= rows) continue;
+        float2* dst = peers[c >> log2_dc] + (c & dmask) * dst_ld + dst_off + r;
+        if (r + 1 < rows && !(reinterpret_cast<uintptr_t>(dst) & 15)) {
+            *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(&t[cl][2 * tx]);
+        } else {
+            dst[0] = t[cl][2 * tx];
+            if (r + 1 < rows) dst[1] = t[cl][2 * tx + 1];
         }
     }
     __threadfence_system();
@@ -150,9 +158,9 @@ int ilog2(int64_t v) {
 cudaError_t launch_scatter(const float2* in, float2* const* peers, int64_t rows, int64_t cols, int64_t dc,
                            int64_t dst_ld, int64_t dst_off, const TwoLevel& tw, int use_tw, uint32_t row0, int conj,
                            float scale, cudaStream_t s) {
-    const int64_t tr = (rows + kTT - 1) / kTT, tc = (cols + kTT - 1) / kTT;
-    k_scatter_transpose<<<(unsigned)(tr * tc), dim3(kTT, 8), 0, s>>>(in, peers, rows, cols, tc, ilog2(dc), dst_ld,
-                                                                     dst_off, tw, use_tw, row0, conj, scale);
+    const int64_t tr = (rows + kSR - 1) / kSR, tc = (cols + kSC - 1) / kSC;
+    k_scatter_transpose<<<(unsigned)(tr * tc), dim3(32, 8), 0, s>>>(in, peers, rows, cols, tc, ilog2(dc), dst_ld,
+                                                                    dst_off, tw, use_tw, row0, conj, scale);
     count_launches(1);
     return cudaGetLastError();
 }
