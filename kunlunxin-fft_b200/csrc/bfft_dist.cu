@@ -139,7 +139,6 @@ __global__ void __launch_bounds__(256) k_scatter_transpose(const float2* __restr
     __threadfence_system();
 }
 
-int g_sms = 0;
 
 cudaError_t launch_transpose(const float2* in, float2* out, int64_t rows, int64_t cols, const TwoLevel& tw,
                              int use_tw, uint32_t row0, int conj, float scale, cudaStream_t s) {
@@ -167,14 +166,12 @@ cudaError_t launch_scatter(const float2* in, float2* const* peers, int64_t rows,
 
 cudaError_t launch_chunk_permute(const float2* in, float2* out, int64_t A, int64_t B, int64_t C, int conj,
                                  float scale, cudaStream_t s) {
-    if (g_sms == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_sms <= 0) g_sms = 148;
-    }
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = device_sm_count(dev, &sms);
+    if (e != cudaSuccess) return e;
     const int64_t total_c = A * B * C;
-    const int blocks_cap = g_sms * 8;
+    const int blocks_cap = sms * 8;
     if (C % 2 == 0) {
         const int64_t total = total_c / 2;
         int64_t grid = (total + 255) / 256;

@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <atomic>
 #include <mutex>
 
 #include "bfft_kernels.cuh"
@@ -725,7 +726,47 @@ __global__ void __launch_bounds__(PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>::THREADS,
     }
 }
 
-static int g_num_sms = 0;
+// Per-device launch facts (SM count, resident CTAs or clusters per kernel
+// configuration), filled on first use under a mutex and read lock-free after.
+static std::mutex g_sm_mu, g_occ_mu;
+static std::atomic<int> g_sm_count[64];
+
+template <typename F>
+static cudaError_t cached_value(std::mutex& mu, std::atomic<int>& slot, int* out, F fill) {
+    int v = slot.load(std::memory_order_acquire);
+    if (v <= 0) {
+        std::lock_guard<std::mutex> lk(mu);
+        v = slot.load(std::memory_order_relaxed);
+        if (v <= 0) {
+            int nv = 0;
+            const cudaError_t e = fill(&nv);
+            if (e != cudaSuccess) return e;
+            v = nv > 0 ? nv : 1;
+            slot.store(v, std::memory_order_release);
+        }
+    }
+    *out = v;
+    return cudaSuccess;
+}
+
+cudaError_t device_sm_count(int dev, int* sms) {
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    return cached_value(g_sm_mu, g_sm_count[dev], sms, [&](int* v) {
+        return cudaDeviceGetAttribute(v, cudaDevAttrMultiProcessorCount, dev);
+    });
+}
+
+// Resident CTAs per SM of `kern` with `smem` dynamic bytes (cached in `slot`).
+template <typename K>
+static cudaError_t cached_occupancy(std::atomic<int>& slot, K kern, int threads, size_t smem, size_t smem_attr,
+                                    int* out) {
+    return cached_value(g_occ_mu, slot, out, [&](int* v) {
+        cudaError_t e = cudaSuccess;
+        if (smem_attr > 48 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_attr);
+        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(v, kern, threads, smem);
+        return e;
+    });
+}
 
 template <int LOG2L, int LAYOUT, int LMAP, int SMAP>
 static cudaError_t launch_pass_t(const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
@@ -735,7 +776,7 @@ static cudaError_t launch_pass_t(const float2* in, float2* out, const PassArgs& 
     // class c holds 2^c entries; occupancy is cached per device and class.
     constexpr int kTw2MaxLog2 = 12;
     constexpr size_t kSmemCap = 227 * 1024;
-    static int blocks_per_sm[64][kTw2MaxLog2 + 2] = {};
+    static std::atomic<int> blocks_per_sm[64][kTw2MaxLog2 + 2];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -754,22 +795,12 @@ static cudaError_t launch_pass_t(const float2* in, float2* out, const PassArgs& 
         }
     }
     const size_t smem_cls = G::SMEM + (cls ? ((size_t)sizeof(float2) << (cls - 1)) : 0);
-    if (blocks_per_sm[dev][cls] == 0) {
-        if (smem_cls > 48 * 1024) {
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
-            if (e != cudaSuccess) return e;
-        }
-        int nb = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, G::THREADS, smem_cls);
-        if (e != cudaSuccess) return e;
-        if (g_num_sms == 0) {
-            e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-            if (e != cudaSuccess) return e;
-        }
-        blocks_per_sm[dev][cls] = nb > 0 ? nb : 1;
-    }
+    int sms = 0, nb = 0;
+    e = device_sm_count(dev, &sms);
+    if (e == cudaSuccess) e = cached_occupancy(blocks_per_sm[dev][cls], kern, G::THREADS, smem_cls, kSmemCap, &nb);
+    if (e != cudaSuccess) return e;
     const int64_t ntiles = (b.nsub + G::K - 1) / G::K;
-    int64_t grid = (int64_t)blocks_per_sm[dev][cls] * g_num_sms;
+    int64_t grid = (int64_t)nb * sms;
     if (grid > ntiles) grid = ntiles;
     if (grid < 1) grid = 1;
     const size_t smem = G::SMEM + (size_t)b.tw_smem_entries * sizeof(float2);
@@ -953,7 +984,7 @@ template <int LOG2N1, int LOG2N2, int LOG2P>
 static cudaError_t launch_cluster_t(const float2* in, float2* out, const ClusterArgs& a, cudaStream_t s) {
     using G = CluGeo<LOG2N1, LOG2N2, LOG2P>;
     auto kern = k_cluster_fft<LOG2N1, LOG2N2, LOG2P>;
-    static int max_clusters[64] = {0};
+    static std::atomic<int> max_clusters[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -969,23 +1000,20 @@ static cudaError_t launch_cluster_t(const float2* in, float2* out, const Cluster
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (max_clusters[dev] == 0) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::SMEM);
-        if (e != cudaSuccess) return e;
-        if (G::P > 8) {
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-            if (e != cudaSuccess) return e;
-        }
-        int sms = 0;
-        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-        cfg.gridDim = dim3((unsigned)(G::P * sms));
-        int nc = 0;
-        e = cudaOccupancyMaxActiveClusters(&nc, kern, &cfg);
-        if (e != cudaSuccess) return e;
-        max_clusters[dev] = nc > 0 ? nc : 1;
-    }
-    int64_t nclu = max_clusters[dev];
+    int sms = 0, nc = 0;
+    e = device_sm_count(dev, &sms);
+    if (e == cudaSuccess)
+        e = cached_value(g_occ_mu, max_clusters[dev], &nc, [&](int* v) {
+            cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::SMEM);
+            if (e2 == cudaSuccess && G::P > 8)
+                e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            cudaLaunchConfig_t q = cfg;
+            q.gridDim = dim3((unsigned)(G::P * sms));
+            if (e2 == cudaSuccess) e2 = cudaOccupancyMaxActiveClusters(v, kern, &q);
+            return e2;
+        });
+    if (e != cudaSuccess) return e;
+    int64_t nclu = nc;
     if (nclu > a.batch) nclu = a.batch;
     cfg.gridDim = dim3((unsigned)(nclu * G::P));
     e = cudaLaunchKernelEx(&cfg, kern, in, out, a);

@@ -67,6 +67,9 @@ cudaError_t launch_cluster_fft(int log2n, const float2* in, float2* out, const C
 // mbarrier wait of the TMA pass); read synchronously, optionally cleared.
 cudaError_t read_device_status(unsigned* status, bool clear);
 
+// SM count of `dev`, cached after the first query (thread-safe).
+cudaError_t device_sm_count(int dev, int* sms);
+
 // Library-wide error message (bfft_last_error) and launch counter.
 void set_last_error(const char* msg);
 void count_launches(int k);

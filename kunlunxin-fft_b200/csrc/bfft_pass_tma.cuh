@@ -457,7 +457,7 @@ static cudaError_t launch_pass_tma_t(const float2* in, float2* out, const PassAr
     auto kern = k_pass_tma<LOG2L, ROWS>;
     constexpr int kTw2MaxLog2 = 12;
     constexpr size_t kSmemCap = 227 * 1024;
-    static int blocks_per_sm[64][kTw2MaxLog2 + 2] = {};
+    static std::atomic<int> blocks_per_sm[64][kTw2MaxLog2 + 2];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -487,20 +487,12 @@ static cudaError_t launch_pass_tma_t(const float2* in, float2* out, const PassAr
         }
     }
     const size_t smem_cls = G::SMEM + (cls ? ((size_t)sizeof(float2) << (cls - 1)) : 0);
-    if (blocks_per_sm[dev][cls] == 0) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
-        if (e != cudaSuccess) return e;
-        int nb = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, G::THREADS, smem_cls);
-        if (e != cudaSuccess) return e;
-        if (g_num_sms == 0) {
-            e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-            if (e != cudaSuccess) return e;
-        }
-        blocks_per_sm[dev][cls] = nb > 0 ? nb : 1;
-    }
+    int sms = 0, nb = 0;
+    e = device_sm_count(dev, &sms);
+    if (e == cudaSuccess) e = cached_occupancy(blocks_per_sm[dev][cls], kern, G::THREADS, smem_cls, kSmemCap, &nb);
+    if (e != cudaSuccess) return e;
     const int64_t ntiles = b.nsub / G::K;
-    int64_t grid = (int64_t)blocks_per_sm[dev][cls] * g_num_sms;
+    int64_t grid = (int64_t)nb * sms;
     if (grid > ntiles) grid = ntiles;
     if (grid < 1) grid = 1;
     const size_t smem = G::SMEM + (size_t)b.tw_smem_entries * sizeof(float2);
@@ -515,7 +507,7 @@ static cudaError_t launch_pass_tma_rows_t(const float2* in, float2* out, const P
     auto kern = k_pass_tma_rows<LOG2L>;
     constexpr int kTw2MaxLog2 = 12;
     constexpr size_t kSmemCap = 227 * 1024;
-    static int blocks_per_sm[64][kTw2MaxLog2 + 2] = {};
+    static std::atomic<int> blocks_per_sm[64][kTw2MaxLog2 + 2];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -534,20 +526,12 @@ static cudaError_t launch_pass_tma_rows_t(const float2* in, float2* out, const P
         }
     }
     const size_t smem_cls = G::SMEM + (cls ? ((size_t)sizeof(float2) << (cls - 1)) : 0);
-    if (blocks_per_sm[dev][cls] == 0) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
-        if (e != cudaSuccess) return e;
-        int nb = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, G::THREADS, smem_cls);
-        if (e != cudaSuccess) return e;
-        if (g_num_sms == 0) {
-            e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-            if (e != cudaSuccess) return e;
-        }
-        blocks_per_sm[dev][cls] = nb > 0 ? nb : 1;
-    }
+    int sms = 0, nb = 0;
+    e = device_sm_count(dev, &sms);
+    if (e == cudaSuccess) e = cached_occupancy(blocks_per_sm[dev][cls], kern, G::THREADS, smem_cls, kSmemCap, &nb);
+    if (e != cudaSuccess) return e;
     const int64_t ntiles = (b.nsub + G::K - 1) / G::K;
-    int64_t grid = (int64_t)blocks_per_sm[dev][cls] * g_num_sms;
+    int64_t grid = (int64_t)nb * sms;
     if (grid > ntiles) grid = ntiles;
     if (grid < 1) grid = 1;
     const size_t smem = G::SMEM + (size_t)b.tw_smem_entries * sizeof(float2);

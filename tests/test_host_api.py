@@ -324,3 +324,62 @@ def test_local_matrix_decomposition_is_a_dft():
         lo, hi = blk[:, :h], blk[:, h:] * w
         state = np.concatenate((lo + hi, lo - hi), axis=1).reshape(n)
     np.testing.assert_allclose(state, np.fft.fft(x), atol=1e-9)
+
+
+def test_host_io_chunking_and_argument_checks():
+    """Host-buffer execution: power-of-two chunk counts dividing the batch,
+    ~64 MiB chunks; shape / dtype / device checks before anything runs."""
+    import torch
+
+    from bfft.entry import ExecutionPlan
+    from bfft.host_io import default_chunks, execute_fft_plan_host
+
+    def plan(n, b, tt="c2c"):
+        return ExecutionPlan(n=n, batch=b, direction="dit", precision="fp32", selection_source="table", reason="t",
+                             fallback=False, executed="fft_dit_matrix_batch" if b > 1 else "fft_dit_matrix",
+                             block=256, params={"tile": min(n, 256)}, transform_type=tt,
+                             transform_direction="inverse" if tt == "c2r" else "forward")
+    assert default_chunks(plan(65536, 8192)) == 64     # 4 GiB -> 64 x 64 MiB
+    assert default_chunks(plan(2048, 1)) == 1
+    assert default_chunks(plan(1024, 48)) == 1        # 384 KiB: one chunk
+    assert default_chunks(plan(1 << 20, 96)) == 8     # 768 MiB -> 12 wanted, largest power of two dividing 96 <= 12
+    p = plan(1024, 16)
+    with pytest.raises(TypeError):
+        execute_fft_plan_host(p, torch.zeros(16, 1024, dtype=torch.complex128))
+    with pytest.raises(ValueError):
+        execute_fft_plan_host(p, torch.zeros(8, 1024, dtype=torch.complex64))
+    with pytest.raises(TypeError):
+        execute_fft_plan_host(p, [0.0])
+
+
+def test_distributed_exchange_mode_validation():
+    from bfft import dist as bdist
+
+    class Stub:
+        def empty(self, count):
+            import torch
+            return torch.empty(count, dtype=torch.complex64)
+
+        def phase(self, k, x, out):
+            out.copy_(x)
+
+    f = bdist.DistributedFFT(256, n1=16, phases=Stub())
+    assert f.exchange == "nccl"
+    with pytest.raises(ValueError):
+        bdist.DistributedFFT(256, n1=16, phases=Stub(), exchange="shm")
+
+
+def test_composition_table_tamper_is_refused(tmp_path):
+    import copy
+
+    from bfft import composition
+
+    t = composition.load_composition_table()
+    if t is None:
+        pytest.skip("no composition table promoted")
+    bad = copy.deepcopy(t)
+    bad["entries"][0]["candidate_ms"] *= 0.5
+    path = tmp_path / "comp.json"
+    path.write_text(json.dumps(bad))
+    with pytest.raises(ConfigError):
+        composition.load_composition_table(str(path))
