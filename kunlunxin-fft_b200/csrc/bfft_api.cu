@@ -107,14 +107,24 @@ cudaError_t alloc_two_level(int64_t n, TwAlloc& t) {
     if (lo_bits < 1) lo_bits = 1;
     int64_t nlo = (int64_t)1 << (lo_bits < log2n ? lo_bits : log2n);
     int64_t nhi = log2n > lo_bits ? ((int64_t)1 << (log2n - lo_bits)) : 1;
-    cudaError_t e = cudaMalloc(&t.mem, sizeof(float2) * (size_t)(nlo + nhi));
+    // beyond 2^22 points the two-level table no longer fits in shared
+    // memory; a three-level one (3 x 2^ceil(log2 N / 3) entries) does
+    const int l3_bits = log2n > 22 ? (log2n + 2) / 3 : 0;
+    const int64_t n3 = l3_bits ? (int64_t)3 << l3_bits : 0;
+    cudaError_t e = cudaMalloc(&t.mem, sizeof(float2) * (size_t)(nlo + nhi + n3));
     if (e != cudaSuccess) return e;
     t.tw.lo = t.mem;
     t.tw.hi = t.mem + nlo;
     t.tw.lo_bits = lo_bits;
     t.tw.log2n = log2n;
     if (log2n == 0) return cudaMemset(t.mem, 0, sizeof(float2));  // W_1 unused
-    return fill_two_level(t.mem, t.mem + nlo, lo_bits, log2n, 0);
+    e = fill_two_level(t.mem, t.mem + nlo, lo_bits, log2n, 0);
+    if (e == cudaSuccess && l3_bits) {
+        t.tw.l3 = t.mem + nlo + nhi;
+        t.tw.l3_bits = l3_bits;
+        e = fill_three_level(t.mem + nlo + nhi, l3_bits, log2n, 0);
+    }
+    return e;
 }
 
 Step stage2(bool dif, int64_t n, int64_t batch, int64_t half, int in_perm, int out_perm,

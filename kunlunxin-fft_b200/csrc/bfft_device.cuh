@@ -157,6 +157,11 @@ struct TwoLevel {
     const float2* hi;
     int lo_bits;
     int log2n;
+    // Optional three-level form of the same W_N (N > 2^22): level j = 0, 1, 2
+    // holds 2^l3_bits entries at l3 + j * 2^l3_bits, entry k of level j being
+    // W_N^{k 2^(j l3_bits)} -- small enough to stage in shared memory.
+    const float2* l3 = nullptr;
+    int l3_bits = 0;
 };
 
 // Exponents are taken mod N (N | 2^32), so 32-bit wrap-around arithmetic on

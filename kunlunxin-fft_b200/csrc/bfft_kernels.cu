@@ -52,6 +52,23 @@ __global__ void k_twiddle_two_level(float2* lo, float2* hi, int lo_bits, int log
     }
 }
 
+__global__ void k_twiddle_three_level(float2* t, int bits, int log2n) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= ((int64_t)3 << bits)) return;
+    const int j = (int)(idx >> bits);
+    const int64_t k = idx & (((int64_t)1 << bits) - 1);
+    const int64_t e = (k << (bits * j)) & ((((int64_t)1) << log2n) - 1);
+    double s, c;
+    sincospi(2.0 * (double)e / (double)((int64_t)1 << log2n), &s, &c);
+    t[idx] = make_float2((float)c, (float)(-s));
+}
+
+cudaError_t fill_three_level(float2* t, int bits, int log2n, cudaStream_t s) {
+    const int64_t tot = (int64_t)3 << bits;
+    k_twiddle_three_level<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(t, bits, log2n);
+    return cudaGetLastError();
+}
+
 static std::mutex g_tw_mu;
 static bool g_tw_ready[64];
 
@@ -567,6 +584,114 @@ __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_g
 // SMAP 0: stores straight from registers;
 // SMAP 1: stores staged through shared memory, element index fastest;
 // SMAP 2: staged, sub-FFT index fastest (coalesced strided columns).
+// W_N lookups for the pre/post twiddles of a pass.  The launcher decides
+// (PassArgs::tw_smem_levels) where the table lives: 2 -- the plan's two-level
+// table staged in shared memory (N <= 2^22), 3 -- its three-level table staged
+// (larger N: one more complex multiply instead of global-memory latency), 0 --
+// the two-level table read from global memory.  The form is a compile-time
+// choice so the unrolled lookups stay branch-free.  The first (low) table is
+// padded by one entry per 16 so lanes striding through it by powers of two
+// spread over the banks.
+__host__ __device__ __forceinline__ int tw_pad(int i) { return i + (i >> 4); }
+
+template <int LEVELS>
+struct SmemTwiddle;
+
+template <>
+struct SmemTwiddle<2> {  // two-level: staged when tw_smem_levels == 2, else global
+    const float2* lo;
+    const float2* hi;
+    uint32_t nmask, lo_mask;
+    int lo_bits;
+    bool staged, split;
+    TwoLevel g;
+
+    // Every thread of the block calls it; the caller's next barrier publishes the table.
+    __device__ void setup(float2* smem, const PassArgs& a) {
+        g = a.tw;
+        staged = a.tw_smem_levels == 2;
+        lo_bits = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
+        split = a.tw.log2n > lo_bits;
+        lo_mask = (1u << lo_bits) - 1u;
+        nmask = a.tw.log2n >= 32 ? 0xffffffffu : (1u << a.tw.log2n) - 1u;
+        const int nlo = 1 << lo_bits, nhi = split ? 1 << (a.tw.log2n - lo_bits) : 0;
+        lo = smem;
+        hi = smem + tw_pad(nlo);
+        if (staged) {
+            for (int i = threadIdx.x; i < nlo; i += blockDim.x) smem[tw_pad(i)] = a.tw.lo[i];
+            for (int i = threadIdx.x; i < nhi; i += blockDim.x) smem[tw_pad(nlo) + i] = a.tw.hi[i];
+        }
+    }
+    __device__ __forceinline__ float2 operator()(uint32_t e) const {
+        if (!staged) return tw_two_level(g, e);
+        e &= nmask;
+        const uint32_t li = e & lo_mask;
+        const float2 w = lo[tw_pad((int)li)];
+        return split ? cmul(w, hi[e >> lo_bits]) : w;
+    }
+};
+
+template <>
+struct SmemTwiddle<3> {  // three-level, always staged
+    const float2* t0;
+    const float2* t1;
+    const float2* t2;
+    uint32_t nmask, mask;
+    int bits;
+
+    __device__ void setup(float2* smem, const PassArgs& a) {
+        bits = a.tw.l3_bits;
+        nmask = a.tw.log2n >= 32 ? 0xffffffffu : (1u << a.tw.log2n) - 1u;
+        mask = (1u << bits) - 1u;
+        const int nb = 1 << bits, stride = tw_pad(nb);
+        t0 = smem;
+        t1 = smem + stride;
+        t2 = smem + 2 * stride;
+        for (int i = threadIdx.x; i < 3 * nb; i += blockDim.x)
+            smem[(i >> bits) * stride + tw_pad(i & (nb - 1))] = a.tw.l3[i];
+    }
+    __device__ __forceinline__ float2 operator()(uint32_t e) const {
+        e &= nmask;
+        const float2 w0 = t0[tw_pad((int)(e & mask))];
+        const float2 w1 = t1[tw_pad((int)((e >> bits) & mask))];
+        const float2 w2 = t2[tw_pad((int)(e >> (2 * bits)))];
+        return cmul(cmul(w0, w1), w2);
+    }
+};
+
+// Shared-memory entries the staged tables of `tw` take (0: no such table).
+inline int tw_smem_entries_for(const TwoLevel& tw, int levels) {
+    if (levels == 2) {
+        const int lob = tw.lo_bits < tw.log2n ? tw.lo_bits : tw.log2n;
+        return tw_pad(1 << lob) + (tw.log2n > lob ? 1 << (tw.log2n - lob) : 0);
+    }
+    if (levels == 3 && tw.l3 && tw.l3_bits > 0) return 3 * tw_pad(1 << tw.l3_bits);
+    return 0;
+}
+
+// Staged form for a pass whose fixed shared memory is `base` bytes: the
+// two-level table when it takes <= 4096 entries, else (when the kernel has a
+// three-level form, max_levels 3) the three-level one, else none; `cls` is
+// the occupancy-cache class (0 = nothing staged).
+inline void choose_tw_staging(PassArgs& pa, size_t base, size_t cap, int& cls, int max_levels = 2) {
+    pa.tw_smem_entries = 0;
+    pa.tw_smem_levels = 0;
+    cls = 0;
+    if (pa.tw_mode == 0) return;
+    for (int levels = 2; levels <= max_levels; ++levels) {
+        const int n = tw_smem_entries_for(pa.tw, levels);
+        if (n <= 0) continue;
+        int c = 0;
+        while ((1 << c) < n) ++c;
+        if (c <= 12 && base + ((size_t)sizeof(float2) << c) <= cap) {
+            pa.tw_smem_entries = n;
+            pa.tw_smem_levels = levels;
+            cls = c + 1;
+            return;
+        }
+    }
+}
+
 template <int LOG2L, int LAYOUT, int LMAP, int SMAP>
 struct PassKGeo {
     static constexpr int L = 1 << LOG2L;
@@ -598,27 +723,9 @@ __global__ void __launch_bounds__(PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>::THREADS,
     int64_t* sbase = reinterpret_cast<int64_t*>(smem + 2 * G::K * G::LPAD);
     float2* tw_smem = reinterpret_cast<float2*>(sbase + G::K);
     fill_stockham_twiddles<LOG2L>(tw_smem);  // visible after the first in-loop barrier
-    // The plan's two-level W_N tables, copied to shared memory when they fit
-    // (launch_pass decides): pre/post twiddles then cost two shared loads.
-    float2* tw2 = tw_smem + tw_total(LOG2L);
-    const bool tws = a.tw_smem_entries > 0;
-    const int lo_bits = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
-    const uint32_t lo_mask = (1u << lo_bits) - 1u;
-    if (tws) {
-        const int nlo = 1 << lo_bits, nhi = a.tw.log2n > lo_bits ? 1 << (a.tw.log2n - lo_bits) : 0;
-        for (int i = threadIdx.x; i < nlo; i += blockDim.x) tw2[i + (i >> 4)] = a.tw.lo[i];
-        for (int i = threadIdx.x; i < nhi; i += blockDim.x) tw2[nlo + (nlo >> 4) + i] = a.tw.hi[i];
-        __syncthreads();
-    }
-    const float2* tw2hi = tw2 + (1 << lo_bits) + ((1 << lo_bits) >> 4);
-    const uint32_t nmask = a.tw.log2n >= 32 ? 0xffffffffu : (1u << a.tw.log2n) - 1u;
-    auto twiddle = [&](uint32_t e) -> float2 {
-        if (!tws) return tw_two_level(a.tw, e);
-        e &= nmask;
-        const uint32_t li = e & lo_mask;
-        const float2 w = tw2[li + (li >> 4)];  // lo table padded by one entry per 16: strided lanes spread over banks
-        return a.tw.log2n > lo_bits ? cmul(w, tw2hi[e >> lo_bits]) : w;
-    };
+    SmemTwiddle<2> twiddle;  // W_N lookups, staged in shared memory when they fit
+    twiddle.setup(tw_smem + tw_total(LOG2L), a);
+    if (a.tw_smem_levels) __syncthreads();
     const int tid = threadIdx.x;
     const int cl = LAYOUT ? tid % G::K : tid / G::TF;
     const int t = LAYOUT ? tid / G::K : tid % G::TF;
@@ -782,18 +889,8 @@ static cudaError_t launch_pass_t(const float2* in, float2* out, const PassArgs& 
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     PassArgs b = a;
-    b.tw_smem_entries = 0;
     int cls = 0;
-    if (a.tw_mode != 0) {
-        const int lob = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
-        const int nlo = 1 << lob, nhi = a.tw.log2n > lob ? 1 << (a.tw.log2n - lob) : 0;
-        int c = 0;
-        while ((1 << c) < nlo + (nlo >> 4) + nhi) ++c;
-        if (c <= kTw2MaxLog2 && G::SMEM + ((size_t)sizeof(float2) << c) <= kSmemCap) {
-            b.tw_smem_entries = nlo + (nlo >> 4) + nhi;
-            cls = c + 1;
-        }
-    }
+    choose_tw_staging(b, G::SMEM, kSmemCap, cls);
     const size_t smem_cls = G::SMEM + (cls ? ((size_t)sizeof(float2) << (cls - 1)) : 0);
     int sms = 0, nb = 0;
     e = device_sm_count(dev, &sms);

@@ -15,6 +15,8 @@ const float2* unit_twiddles(int device);
 
 // Two-level table for W_N^e, e < N (plan-owned device memory).
 cudaError_t fill_two_level(float2* lo, float2* hi, int lo_bits, int log2n, cudaStream_t s);
+// Three-level table (3 x 2^bits entries, TwoLevel::l3) for W_N^e, e < N.
+cudaError_t fill_three_level(float2* t, int bits, int log2n, cudaStream_t s);
 
 // ---------------------------------------------------------------- stage kernels
 struct StageArgs {
@@ -108,7 +110,8 @@ struct PassArgs {
     float scale;
     int conj_in, conj_out;
     const float2* unit_tw;  // unit twiddle levels (ensure_unit_twiddles)
-    int tw_smem_entries;    // set by launch_pass: > 0 = the W_N tables are copied to shared memory
+    int tw_smem_entries;    // set by launch_pass: shared-memory entries of the staged W_N tables
+    int tw_smem_levels;     // set by launch_pass: 0 global two-level, 2 / 3 staged two- / three-level
 };
 
 constexpr int kMaxPassLog2 = 12;  // largest CTA-resident sub-FFT: 4096 points

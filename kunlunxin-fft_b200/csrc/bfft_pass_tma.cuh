@@ -141,7 +141,8 @@ struct PassTGeo {
     static_assert(L >= 16 && K <= 256 && LB <= 256, "TMA box limits");
 };
 
-template <int LOG2L, int ROWS>
+// TW3: the pass's W_N twiddles come from the plan's three-level table (N > 2^22).
+template <int LOG2L, int ROWS, bool TW3>
 __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L, ROWS>::MINB)
     k_pass_tma(const __grid_constant__ CUtensorMap tin, const __grid_constant__ CUtensorMap tout,
                float2* __restrict__ out, PassArgs a) {
@@ -151,7 +152,6 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(base + G::STAGES * G::SB);
     float2* tw_smem = reinterpret_cast<float2*>(full + 8);
-    float2* tw2 = tw_smem + tw_total(LOG2L);
     auto stage = [&](int s) { return reinterpret_cast<float2*>(base + s * G::SB); };
 
     const int tid = threadIdx.x;
@@ -163,23 +163,8 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
     const bool scaled = a.scale != 1.0f || a.conj_out;  // uniform: skip the epilogue multiply when it is 1
 
     fill_stockham_twiddles<LOG2L>(tw_smem);
-    const bool tws = a.tw_smem_entries > 0;
-    const int lo_bits = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
-    const uint32_t lo_mask = (1u << lo_bits) - 1u;
-    if (tws) {
-        const int nlo = 1 << lo_bits, nhi = a.tw.log2n > lo_bits ? 1 << (a.tw.log2n - lo_bits) : 0;
-        for (int i = tid; i < nlo; i += blockDim.x) tw2[i + (i >> 4)] = a.tw.lo[i];
-        for (int i = tid; i < nhi; i += blockDim.x) tw2[nlo + (nlo >> 4) + i] = a.tw.hi[i];
-    }
-    const float2* tw2hi = tw2 + (1 << lo_bits) + ((1 << lo_bits) >> 4);
-    const uint32_t nmask = a.tw.log2n >= 32 ? 0xffffffffu : (1u << a.tw.log2n) - 1u;
-    auto twiddle = [&](uint32_t e) -> float2 {
-        if (!tws) return tw_two_level(a.tw, e);
-        e &= nmask;
-        const uint32_t li = e & lo_mask;
-        const float2 w = tw2[li + (li >> 4)];  // lo table padded by one entry per 16: strided lanes spread over banks
-        return a.tw.log2n > lo_bits ? cmul(w, tw2hi[e >> lo_bits]) : w;
-    };
+    SmemTwiddle<TW3 ? 3 : 2> twiddle;  // W_N lookups, staged in shared memory when they fit
+    twiddle.setup(tw_smem + tw_total(LOG2L), a);
     if (tid == 0) {
         for (int s = 0; s < G::STAGES; ++s) mbar_init(&full[s], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -302,7 +287,6 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(base + G::STAGES * G::SB);
     float2* tw_smem = reinterpret_cast<float2*>(full + 8);
-    float2* tw2 = tw_smem + tw_total(LOG2L);
     auto stage = [&](int s) { return reinterpret_cast<float2*>(base + s * G::SB); };
 
     const int tid = threadIdx.x;
@@ -314,23 +298,8 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
     const int NST = out_contig ? 1 : G::K;  // threads that issue (and wait for) stores
 
     fill_stockham_twiddles<LOG2L>(tw_smem);
-    const bool tws = a.tw_smem_entries > 0;
-    const int lo_bits = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
-    const uint32_t lo_mask = (1u << lo_bits) - 1u;
-    if (tws) {
-        const int nlo = 1 << lo_bits, nhi = a.tw.log2n > lo_bits ? 1 << (a.tw.log2n - lo_bits) : 0;
-        for (int i = tid; i < nlo; i += blockDim.x) tw2[i + (i >> 4)] = a.tw.lo[i];
-        for (int i = tid; i < nhi; i += blockDim.x) tw2[nlo + (nlo >> 4) + i] = a.tw.hi[i];
-    }
-    const float2* tw2hi = tw2 + (1 << lo_bits) + ((1 << lo_bits) >> 4);
-    const uint32_t nmask = a.tw.log2n >= 32 ? 0xffffffffu : (1u << a.tw.log2n) - 1u;
-    auto twiddle = [&](uint32_t e) -> float2 {
-        if (!tws) return tw_two_level(a.tw, e);
-        e &= nmask;
-        const uint32_t li = e & lo_mask;
-        const float2 w = tw2[li + (li >> 4)];  // lo table padded by one entry per 16: strided lanes spread over banks
-        return a.tw.log2n > lo_bits ? cmul(w, tw2hi[e >> lo_bits]) : w;
-    };
+    SmemTwiddle<2> twiddle;  // W_N lookups, staged in shared memory when they fit
+    twiddle.setup(tw_smem + tw_total(LOG2L), a);
     auto row_in = [&](int64_t f) -> const float2* {
         const int64_t o = f >> a.inner_log2, c = f & imask;
         const int64_t cin = a.in_base_bits ? (int64_t)brev_bits((uint32_t)c, a.in_base_bits) : c;
@@ -454,10 +423,9 @@ static bool encode_map_3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t
 template <int LOG2L, int ROWS>
 static cudaError_t launch_pass_tma_t(const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
     using G = PassTGeo<LOG2L, ROWS>;
-    auto kern = k_pass_tma<LOG2L, ROWS>;
     constexpr int kTw2MaxLog2 = 12;
     constexpr size_t kSmemCap = 227 * 1024;
-    static std::atomic<int> blocks_per_sm[64][kTw2MaxLog2 + 2];
+    static std::atomic<int> blocks_per_sm[64][2][kTw2MaxLog2 + 2];  // [device][three-level][class]
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -474,29 +442,27 @@ static cudaError_t launch_pass_tma_t(const float2* in, float2* out, const PassAr
         return cudaErrorNotSupported;
     }
     PassArgs b = a;
-    b.tw_smem_entries = 0;
     int cls = 0;
-    if (a.tw_mode != 0) {
-        const int lob = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
-        const int nlo = 1 << lob, nhi = a.tw.log2n > lob ? 1 << (a.tw.log2n - lob) : 0;
-        int c = 0;
-        while ((1 << c) < nlo + (nlo >> 4) + nhi) ++c;
-        if (c <= kTw2MaxLog2 && G::SMEM + ((size_t)sizeof(float2) << c) <= kSmemCap) {
-            b.tw_smem_entries = nlo + (nlo >> 4) + nhi;
-            cls = c + 1;
-        }
-    }
+    choose_tw_staging(b, G::SMEM, kSmemCap, cls, 3);
+    const bool tw3 = b.tw_smem_levels == 3;
     const size_t smem_cls = G::SMEM + (cls ? ((size_t)sizeof(float2) << (cls - 1)) : 0);
     int sms = 0, nb = 0;
     e = device_sm_count(dev, &sms);
-    if (e == cudaSuccess) e = cached_occupancy(blocks_per_sm[dev][cls], kern, G::THREADS, smem_cls, kSmemCap, &nb);
+    if (e == cudaSuccess)
+        e = tw3 ? cached_occupancy(blocks_per_sm[dev][1][cls], k_pass_tma<LOG2L, ROWS, true>, G::THREADS, smem_cls,
+                                   kSmemCap, &nb)
+                : cached_occupancy(blocks_per_sm[dev][0][cls], k_pass_tma<LOG2L, ROWS, false>, G::THREADS, smem_cls,
+                                   kSmemCap, &nb);
     if (e != cudaSuccess) return e;
     const int64_t ntiles = b.nsub / G::K;
     int64_t grid = (int64_t)nb * sms;
     if (grid > ntiles) grid = ntiles;
     if (grid < 1) grid = 1;
     const size_t smem = G::SMEM + (size_t)b.tw_smem_entries * sizeof(float2);
-    kern<<<(unsigned)grid, G::THREADS, smem, s>>>(tin, tout, out, b);
+    if (tw3)
+        k_pass_tma<LOG2L, ROWS, true><<<(unsigned)grid, G::THREADS, smem, s>>>(tin, tout, out, b);
+    else
+        k_pass_tma<LOG2L, ROWS, false><<<(unsigned)grid, G::THREADS, smem, s>>>(tin, tout, out, b);
     return cudaGetLastError();
 }
 
@@ -513,18 +479,8 @@ static cudaError_t launch_pass_tma_rows_t(const float2* in, float2* out, const P
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     PassArgs b = a;
-    b.tw_smem_entries = 0;
     int cls = 0;
-    if (a.tw_mode != 0) {
-        const int lob = a.tw.lo_bits < a.tw.log2n ? a.tw.lo_bits : a.tw.log2n;
-        const int nlo = 1 << lob, nhi = a.tw.log2n > lob ? 1 << (a.tw.log2n - lob) : 0;
-        int c = 0;
-        while ((1 << c) < nlo + (nlo >> 4) + nhi) ++c;
-        if (c <= kTw2MaxLog2 && G::SMEM + ((size_t)sizeof(float2) << c) <= kSmemCap) {
-            b.tw_smem_entries = nlo + (nlo >> 4) + nhi;
-            cls = c + 1;
-        }
-    }
+    choose_tw_staging(b, G::SMEM, kSmemCap, cls);
     const size_t smem_cls = G::SMEM + (cls ? ((size_t)sizeof(float2) << (cls - 1)) : 0);
     int sms = 0, nb = 0;
     e = device_sm_count(dev, &sms);
