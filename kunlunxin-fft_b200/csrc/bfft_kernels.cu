@@ -478,8 +478,17 @@ __host__ __device__ constexpr int radix_log2(int log2l, int pass) { return pass 
 // p > 1, rows k < p of R-1 entries W_{Rp}^{j k} (j = 1..R-1).  The odd row
 // stride R-1 keeps consecutive k on distinct banks; a thread's row depends
 // only on its index, so a persistent CTA fills the tables once.
+// Pass 2 (p = 256) of radix R >= 4 keeps two 16-row tables instead of one
+// 256-row table: with k = 16 kh + kl, W_{256 R}^{j k} = W_{256 R}^{j kl}
+// W_{16 R}^{j kh} (one more complex multiply, 8-16x less shared memory --
+// what lets three CTAs of the 1024..4096-point passes share an SM).
+__host__ __device__ constexpr bool tw_split(int log2l, int pass) {
+    return pass == 2 && radix_log2(log2l, pass) >= 2;
+}
 __host__ __device__ constexpr int tw_pass_entries(int log2l, int pass) {
-    return pass == 0 ? 0 : (1 << (4 * pass)) * ((1 << radix_log2(log2l, pass)) - 1);
+    return pass == 0 ? 0
+         : tw_split(log2l, pass) ? 2 * 16 * ((1 << radix_log2(log2l, pass)) - 1)
+                                 : (1 << (4 * pass)) * ((1 << radix_log2(log2l, pass)) - 1);
 }
 __host__ __device__ constexpr int tw_offset(int log2l, int pass) {
     int off = 0;
@@ -495,8 +504,16 @@ __device__ __forceinline__ void fill_stockham_twiddles(float2* tw_smem) {
     constexpr int NP = LOG2L <= 4 ? 1 : (LOG2L + 3) / 4;
     for (int pass = 1; pass < NP; ++pass) {
         const int r = 1 << radix_log2(LOG2L, pass), p = 1 << (4 * pass);
-        const float2* lvl = g_tw_levels + r * p;
         float2* dst = tw_smem + tw_offset(LOG2L, pass);
+        if (tw_split(LOG2L, pass)) {  // rows kl (W_{256 r}^{j kl}) then rows kh (W_{16 r}^{j kh})
+            const int cnt = 2 * 16 * (r - 1);
+            for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+                const int row = i / (r - 1), j = i - row * (r - 1) + 1;
+                dst[i] = row < 16 ? g_tw_levels[r * p + j * row] : g_tw_levels[r * 16 + j * (row - 16)];
+            }
+            continue;
+        }
+        const float2* lvl = g_tw_levels + r * p;
         const int cnt = p * (r - 1);
         for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
             const int k = i / (r - 1), j = i - k * (r - 1) + 1;
@@ -530,7 +547,12 @@ __device__ __forceinline__ void stockham_passes(float2 (&v)[E], int t, float2* r
             float2 u[R];
 #pragma unroll
             for (int j = 0; j < R; ++j) u[j] = v[q + j * NB];
-            if constexpr (PASS > 0) {
+            if constexpr (tw_split(LOG2L, PASS)) {
+                const float2* tl = tw_smem + tw_offset(LOG2L, PASS) + (k & 15) * (R - 1) - 1;
+                const float2* th = tw_smem + tw_offset(LOG2L, PASS) + (16 + (k >> 4)) * (R - 1) - 1;
+#pragma unroll
+                for (int j = 1; j < R; ++j) u[j] = cmul(u[j], cmul(tl[j], th[j]));
+            } else if constexpr (PASS > 0) {
                 const float2* tw = tw_smem + tw_offset(LOG2L, PASS) + k * (R - 1) - 1;
 #pragma unroll
                 for (int j = 1; j < R; ++j) u[j] = cmul(u[j], tw[j]);

@@ -270,10 +270,11 @@ struct PassRGeo {
     static constexpr int K = 256 / TF;  // 256 threads
     static constexpr int THREADS = 256;
     static constexpr int LPAD = (L + (L >> 4)) | 1;
-    static constexpr int SB = ((K * LPAD * 8) + 1023) / 1024 * 1024;
+    // bulk copies need 16-byte alignment only: 128-byte rounding, not 1 KB
+    static constexpr int SB = ((K * LPAD * 8) + 127) / 128 * 128;
     static constexpr int STAGES = 2;
     static constexpr int MINB = 3;
-    static constexpr size_t SMEM = 1024 + (size_t)STAGES * SB + 64 + (size_t)tw_total(LOG2L) * sizeof(float2);
+    static constexpr size_t SMEM = 128 + (size_t)STAGES * SB + 64 + (size_t)tw_total(LOG2L) * sizeof(float2);
     static_assert(L >= 256 && K >= 1, "row tiles need L >= 256");
 };
 
@@ -284,7 +285,7 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
     using G = PassRGeo<LOG2L>;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* base =
-        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     uint64_t* full = reinterpret_cast<uint64_t*>(base + G::STAGES * G::SB);
     float2* tw_smem = reinterpret_cast<float2*>(full + 8);
     auto stage = [&](int s) { return reinterpret_cast<float2*>(base + s * G::SB); };
