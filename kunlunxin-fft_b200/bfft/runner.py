@@ -14,8 +14,9 @@ CUDA stream through the C ABI.  How each flow maps onto B200 kernels:
   pass (the bit reversal folded into its loads), then radix-2 global stages.
 * ``fft_*_matrix[_batch]`` (M2, "batch local-fused core"): the local group of
   log2(tile) stages as one CTA-resident pass; the remaining stages are grouped
-  into the fewest further passes (each up to 4096 points), so N <= 4096 with
-  tile = N is a single HBM round trip and N <= 2^24 is two.
+  into the fewest further column passes of up to 512 points each (the size the
+  TMA-staged column pass covers), so N <= 4096 with tile = N is a single HBM
+  round trip, N <= 2^21 with tile 4096 two, and N = 2^30 with tile 256 four.
 * ``fft_*_grouped`` (M3): the local pass plus the reference's tail partition
   (``tail_groups``): each execution group is one pass, leftovers radix-2 stages.
 
