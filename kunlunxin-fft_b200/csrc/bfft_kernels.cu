@@ -693,8 +693,14 @@ inline int tw_smem_entries_for(const TwoLevel& tw, int levels) {
 
 // Staged form for a pass whose fixed shared memory is `base` bytes: the
 // two-level table when it takes <= 4096 entries, else (when the kernel has a
-// three-level form, max_levels 3) the three-level one, else none; `cls` is
-// the occupancy-cache class (0 = nothing staged).
+// three-level form, max_levels 3) the three-level one, else none.  `cls` is
+// the occupancy-cache class: 0 = nothing staged, else the table rounded up to
+// a multiple of kTwClassEntries entries (fine enough that the rounding never
+// costs a resident CTA).
+constexpr int kTwClassEntries = 64;
+constexpr int kTwClasses = 4096 / kTwClassEntries + 1;  // class 0..64
+inline size_t tw_class_bytes(int cls) { return (size_t)cls * kTwClassEntries * sizeof(float2); }
+
 inline void choose_tw_staging(PassArgs& pa, size_t base, size_t cap, int& cls, int max_levels = 2) {
     pa.tw_smem_entries = 0;
     pa.tw_smem_levels = 0;
@@ -702,13 +708,12 @@ inline void choose_tw_staging(PassArgs& pa, size_t base, size_t cap, int& cls, i
     if (pa.tw_mode == 0) return;
     for (int levels = 2; levels <= max_levels; ++levels) {
         const int n = tw_smem_entries_for(pa.tw, levels);
-        if (n <= 0) continue;
-        int c = 0;
-        while ((1 << c) < n) ++c;
-        if (c <= 12 && base + ((size_t)sizeof(float2) << c) <= cap) {
+        if (n <= 0 || n > 4096) continue;
+        const int c = (n + kTwClassEntries - 1) / kTwClassEntries;
+        if (base + tw_class_bytes(c) <= cap) {
             pa.tw_smem_entries = n;
             pa.tw_smem_levels = levels;
-            cls = c + 1;
+            cls = c;
             return;
         }
     }
@@ -901,11 +906,10 @@ template <int LOG2L, int LAYOUT, int LMAP, int SMAP>
 static cudaError_t launch_pass_t(const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
     using G = PassKGeo<LOG2L, LAYOUT, LMAP, SMAP>;
     auto kern = k_pass<LOG2L, LAYOUT, LMAP, SMAP>;
-    // Shared-memory W_N tables: up to kTw2Max entries (N <= 2^22), size
-    // class c holds 2^c entries; occupancy is cached per device and class.
-    constexpr int kTw2MaxLog2 = 12;
+    // Shared-memory W_N tables: up to 4096 entries (N <= 2^22); occupancy
+    // is cached per device and table size class.
     constexpr size_t kSmemCap = 227 * 1024;
-    static std::atomic<int> blocks_per_sm[64][kTw2MaxLog2 + 2];
+    static std::atomic<int> blocks_per_sm[64][kTwClasses];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -913,7 +917,7 @@ static cudaError_t launch_pass_t(const float2* in, float2* out, const PassArgs& 
     PassArgs b = a;
     int cls = 0;
     choose_tw_staging(b, G::SMEM, kSmemCap, cls);
-    const size_t smem_cls = G::SMEM + (cls ? ((size_t)sizeof(float2) << (cls - 1)) : 0);
+    const size_t smem_cls = G::SMEM + tw_class_bytes(cls);
     int sms = 0, nb = 0;
     e = device_sm_count(dev, &sms);
     if (e == cudaSuccess) e = cached_occupancy(blocks_per_sm[dev][cls], kern, G::THREADS, smem_cls, kSmemCap, &nb);

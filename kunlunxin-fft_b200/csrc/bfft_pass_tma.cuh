@@ -132,12 +132,19 @@ struct PassTGeo {
     static constexpr int THREADS = K * TF;
     static constexpr int LB = L < 256 ? L : 256;  // TMA box extent along the element index
     static constexpr int RPAD = ROWS ? 2 : 0;     // row staging: 16-byte aligned rows, 2-way conflicts at most
-    static constexpr int SB = ((K * (L + RPAD) * 8) + 1023) / 1024 * 1024;
+    // stages start on 128-byte boundaries (TMA destinations without swizzle)
+    static constexpr int SB = ((K * (L + RPAD) * 8) + 127) / 128 * 128;
     // 256-thread CTAs: two stages and <= 85 registers, three CTAs (24 warps)
     // per SM; 512-thread CTAs (L = 512): one per SM, three stages.
     static constexpr int STAGES = THREADS >= 512 ? 3 : 2;
     static constexpr int MINB = THREADS >= 512 ? 1 : 3;
-    static constexpr size_t SMEM = 1024 + (size_t)STAGES * SB + 64 + (size_t)tw_total(LOG2L) * sizeof(float2);
+    // W_N column factors shared by the TF threads of a sub-FFT (TF >= 4):
+    // a [m][sub-FFT] table of 16 x K entries
+    static constexpr bool COLTW = TF >= 4;
+    static constexpr int COLTW_ENTRIES = COLTW ? 16 * K : 0;
+    static constexpr int CPT = TF >= 16 ? 1 : 16 / TF;  // column factors per thread
+    static constexpr size_t SMEM =
+        128 + (size_t)STAGES * SB + 64 + (size_t)(tw_total(LOG2L) + COLTW_ENTRIES) * sizeof(float2);
     static_assert(L >= 16 && K <= 256 && LB <= 256, "TMA box limits");
 };
 
@@ -149,9 +156,10 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
     using G = PassTGeo<LOG2L, ROWS>;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* base =
-        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     uint64_t* full = reinterpret_cast<uint64_t*>(base + G::STAGES * G::SB);
     float2* tw_smem = reinterpret_cast<float2*>(full + 8);
+    float2* coltw = tw_smem + tw_total(LOG2L);
     auto stage = [&](int s) { return reinterpret_cast<float2*>(base + s * G::SB); };
 
     const int tid = threadIdx.x;
@@ -164,13 +172,24 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
 
     fill_stockham_twiddles<LOG2L>(tw_smem);
     SmemTwiddle<TW3 ? 3 : 2> twiddle;  // W_N lookups, staged in shared memory when they fit
-    twiddle.setup(tw_smem + tw_total(LOG2L), a);
+    twiddle.setup(coltw + G::COLTW_ENTRIES, a);
     if (tid == 0) {
         for (int s = 0; s < G::STAGES; ++s) mbar_init(&full[s], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_proxy_async_smem();
     }
     __syncthreads();
+
+    // The W_N twiddle of element e = t + m TF of sub-FFT c is W^{e C} with
+    // C = c tw_mul, i.e. W^{t C} W^{m TF C}.  With TF >= 4 the 16 column
+    // factors W^{m TF C} of a sub-FFT are shared by its TF threads: each
+    // thread computes its share (m = t, t + TF, ...) into the [m][sub-FFT]
+    // table while the tile is still in flight, plus its own W^{t C}: 1 +
+    // max(1, 16/TF) W_N lookups per thread and tile instead of 16.  Thread
+    // t = 0 has W^0 = 1 exactly, so its twiddles are the table's.  The table
+    // is read only between the tile's first barrier and its last one, and
+    // written only before the first.
+    const bool twiddled = a.tw_mode != 0;  // uniform
 
     // bit reversal over log2 L bits of e = t + m TF (t < TF, m < 16) is
     // rev(t) * 16 + rev4(m): a per-thread base plus a constant per element
@@ -194,11 +213,28 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
         float2* buf = stage(s);
         const int64_t f = tile * G::K + cl;
         const int64_t o = f >> a.inner_log2, c = f & imask;
+        const uint32_t cmul32 = static_cast<uint32_t>(c) * static_cast<uint32_t>(a.tw_mul);
+        const float2* cf = coltw + cl;  // this sub-FFT's column factors
+        float2 tb = make_float2(1.f, 0.f);
+        if constexpr (G::COLTW) {
+            if (twiddled) {
+#pragma unroll
+                for (int j = 0; j < G::CPT; ++j) {
+                    const int m = t + j * G::TF;
+                    if (m < 16) coltw[m * G::K + cl] = twiddle(static_cast<uint32_t>(m * G::TF) * cmul32);
+                }
+                tb = twiddle(static_cast<uint32_t>(t) * cmul32);
+            }
+        }
+        // W^{(t + m TF) C}
+        auto wn = [&](int m) {
+            if constexpr (G::COLTW) return cmul(tb, cf[m * G::K]);
+            else return twiddle(static_cast<uint32_t>(t + m * G::TF) * cmul32);
+        };
         // the stores that read the stage the next load will fill (tile it+1-STAGES) are done reading
         if (tid < NST) bulk_wait_read<G::STAGES - 2>();
         const bool ok = mbar_wait_bounded(&full[s], static_cast<uint32_t>((it / G::STAGES) & 1));
 
-        const uint32_t cmul32 = static_cast<uint32_t>(c) * static_cast<uint32_t>(a.tw_mul);
         float2 v[16];
 #pragma unroll
         for (int m = 0; m < 16; ++m) {
@@ -206,14 +242,22 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
             const uint32_t pe = a.in_elem_bitrev ? rt16 + rev4(m) : e;
             float2 val = ok ? buf[pe * G::K + cl] : make_float2(0.f, 0.f);
             if (a.conj_in) val.y = -val.y;
-            if (a.tw_mode == 1) val = cmul(val, twiddle(e * cmul32));
+            if constexpr (!G::COLTW) {
+                if (a.tw_mode == 1) val = cmul(val, wn(m));
+            }
             v[m] = val;
         }
-        if (__syncthreads_or(!ok)) {  // the tile is now the exchange area
+        if (__syncthreads_or(!ok)) {  // the tile is now the exchange area; the column factors are published
             aborted = true;
             break;
         }
         if (tid == 0 && tile + gridDim.x < ntiles) issue(tile + gridDim.x, (it + 1) % G::STAGES);
+        if constexpr (G::COLTW) {
+            if (a.tw_mode == 1) {
+#pragma unroll
+                for (int m = 0; m < 16; ++m) v[m] = cmul(v[m], wn(m));
+            }
+        }
 
         stockham_passes<LOG2L, 0, 16, G::TF, G::K>(v, t, buf + cl, tw_smem);
 
@@ -221,7 +265,7 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
         for (int m = 0; m < 16; ++m) {
             const uint32_t k = static_cast<uint32_t>(t + m * G::TF);
             float2 val = v[m];
-            if (a.tw_mode == 2) val = cmul(val, twiddle(k * cmul32));
+            if (a.tw_mode == 2) val = cmul(val, wn(m));
             if (scaled) val = make_float2(val.x * osr, val.y * osi);
             if constexpr (ROWS) {
                 buf[cl * (G::L + G::RPAD) + k] = val;
@@ -424,9 +468,8 @@ static bool encode_map_3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t
 template <int LOG2L, int ROWS>
 static cudaError_t launch_pass_tma_t(const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
     using G = PassTGeo<LOG2L, ROWS>;
-    constexpr int kTw2MaxLog2 = 12;
     constexpr size_t kSmemCap = 227 * 1024;
-    static std::atomic<int> blocks_per_sm[64][2][kTw2MaxLog2 + 2];  // [device][three-level][class]
+    static std::atomic<int> blocks_per_sm[64][2][kTwClasses];  // [device][three-level][class]
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -446,7 +489,7 @@ static cudaError_t launch_pass_tma_t(const float2* in, float2* out, const PassAr
     int cls = 0;
     choose_tw_staging(b, G::SMEM, kSmemCap, cls, 3);
     const bool tw3 = b.tw_smem_levels == 3;
-    const size_t smem_cls = G::SMEM + (cls ? ((size_t)sizeof(float2) << (cls - 1)) : 0);
+    const size_t smem_cls = G::SMEM + tw_class_bytes(cls);
     int sms = 0, nb = 0;
     e = device_sm_count(dev, &sms);
     if (e == cudaSuccess)
@@ -472,9 +515,8 @@ static cudaError_t launch_pass_tma_rows_t(const float2* in, float2* out, const P
                                           int out_contig, cudaStream_t s) {
     using G = PassRGeo<LOG2L>;
     auto kern = k_pass_tma_rows<LOG2L>;
-    constexpr int kTw2MaxLog2 = 12;
     constexpr size_t kSmemCap = 227 * 1024;
-    static std::atomic<int> blocks_per_sm[64][kTw2MaxLog2 + 2];
+    static std::atomic<int> blocks_per_sm[64][kTwClasses];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -482,7 +524,7 @@ static cudaError_t launch_pass_tma_rows_t(const float2* in, float2* out, const P
     PassArgs b = a;
     int cls = 0;
     choose_tw_staging(b, G::SMEM, kSmemCap, cls);
-    const size_t smem_cls = G::SMEM + (cls ? ((size_t)sizeof(float2) << (cls - 1)) : 0);
+    const size_t smem_cls = G::SMEM + tw_class_bytes(cls);
     int sms = 0, nb = 0;
     e = device_sm_count(dev, &sms);
     if (e == cudaSuccess) e = cached_occupancy(blocks_per_sm[dev][cls], kern, G::THREADS, smem_cls, kSmemCap, &nb);
