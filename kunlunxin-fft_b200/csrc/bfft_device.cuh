@@ -20,6 +20,41 @@ __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
     return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
 }
 __device__ __forceinline__ float2 cconj(float2 a) { return make_float2(a.x, -a.y); }
+
+// Packed FP32x2 forms of cadd / csub (sm_100 `add.rn.f32x2` / `sub.rn.f32x2`):
+// one instruction per complex add, each lane rounded exactly like the scalar
+// add.  Chosen per kernel (the PK parameter of Dft / stockham_passes) by
+// measurement: they pay where the butterflies dominate the instruction count.
+__device__ __forceinline__ unsigned long long pack2(float2 a) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a.x), "f"(a.y));
+    return r;
+}
+__device__ __forceinline__ float2 unpack2(unsigned long long r) {
+    float2 d;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(r));
+    return d;
+}
+template <bool PK>
+__device__ __forceinline__ float2 cadd_p(float2 a, float2 b) {
+    if constexpr (PK) {
+        unsigned long long d;
+        asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack2(a)), "l"(pack2(b)));
+        return unpack2(d);
+    } else {
+        return cadd(a, b);
+    }
+}
+template <bool PK>
+__device__ __forceinline__ float2 csub_p(float2 a, float2 b) {
+    if constexpr (PK) {
+        unsigned long long d;
+        asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack2(a)), "l"(pack2(b)));
+        return unpack2(d);
+    } else {
+        return csub(a, b);
+    }
+}
 __device__ __forceinline__ float2 cscale(float2 a, float s) { return make_float2(a.x * s, a.y * s); }
 
 // Bit reversal of the low `bits` bits (bits in [0, 32]).  Reference index map:
@@ -93,7 +128,8 @@ __device__ __forceinline__ float2 mul_wconst(float2 v) {
 // ---------------------------------------------------------------- in-register DFT
 // Natural-order forward DFT of R values held in registers (R | 16), by
 // radix-2 decimation in time; fully unrolled, all indices compile-time.
-template <int R>
+// PK: complex adds as packed FP32x2 instructions (same results).
+template <int R, bool PK = false>
 struct Dft {
     static __device__ __forceinline__ void run(float2 (&v)[R]) {
         float2 e[R / 2], o[R / 2];
@@ -102,8 +138,8 @@ struct Dft {
             e[i] = v[2 * i];
             o[i] = v[2 * i + 1];
         }
-        Dft<R / 2>::run(e);
-        Dft<R / 2>::run(o);
+        Dft<R / 2, PK>::run(e);
+        Dft<R / 2, PK>::run(o);
         combine<0>(v, e, o);
     }
     template <int K>
@@ -111,34 +147,34 @@ struct Dft {
                                                    const float2 (&o)[R / 2]) {
         if constexpr (K < R / 2) {
             float2 t = mul_wconst<K, R>(o[K]);
-            v[K] = cadd(e[K], t);
-            v[K + R / 2] = csub(e[K], t);
+            v[K] = cadd_p<PK>(e[K], t);
+            v[K + R / 2] = csub_p<PK>(e[K], t);
             combine<K + 1>(v, e, o);
         }
     }
 };
-template <>
-struct Dft<1> {
+template <bool PK>
+struct Dft<1, PK> {
     static __device__ __forceinline__ void run(float2 (&)[1]) {}
 };
-template <>
-struct Dft<2> {
+template <bool PK>
+struct Dft<2, PK> {
     static __device__ __forceinline__ void run(float2 (&v)[2]) {
         float2 a = v[0], b = v[1];
-        v[0] = cadd(a, b);
-        v[1] = csub(a, b);
+        v[0] = cadd_p<PK>(a, b);
+        v[1] = csub_p<PK>(a, b);
     }
 };
-template <>
-struct Dft<4> {
+template <bool PK>
+struct Dft<4, PK> {
     static __device__ __forceinline__ void run(float2 (&v)[4]) {
-        float2 s02 = cadd(v[0], v[2]), d02 = csub(v[0], v[2]);
-        float2 s13 = cadd(v[1], v[3]), d13 = csub(v[1], v[3]);
+        float2 s02 = cadd_p<PK>(v[0], v[2]), d02 = csub_p<PK>(v[0], v[2]);
+        float2 s13 = cadd_p<PK>(v[1], v[3]), d13 = csub_p<PK>(v[1], v[3]);
         float2 d13m = make_float2(d13.y, -d13.x);  // -i * d13
-        v[0] = cadd(s02, s13);
-        v[2] = csub(s02, s13);
-        v[1] = cadd(d02, d13m);
-        v[3] = csub(d02, d13m);
+        v[0] = cadd_p<PK>(s02, s13);
+        v[2] = csub_p<PK>(s02, s13);
+        v[1] = cadd_p<PK>(d02, d13m);
+        v[3] = csub_p<PK>(d02, d13m);
     }
 };
 
