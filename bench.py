@@ -57,7 +57,7 @@ SEED = 1234
 # case of the same flow scaled by the elements processed (the summary under
 # profiles/ gives the command and the raw figures).  Keyed by workload and plan.
 PROFILED_TRAFFIC = {
-    ("5a", "fft_dit_matrix_batch", 256): (7.83e9, "profiles/k_pass_tma_5a.md"),
+    ("5a", "fft_dit_matrix_batch", 256): (7.82e9, "profiles/k_pass_tma_5a.md"),
 }
 FALLBACK_HBM_GBS = 6650.0
 
