@@ -298,14 +298,17 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
     if (tid < NST) bulk_wait<0>();
 }
 
-// ---- row tiles: sub-FFTs whose elements are contiguous (L >= 256) ----
+// ---- row tiles: sub-FFTs whose elements are contiguous (L >= 32) ----
 //
 // A tile is K rows of L points; every row is one bulk copy (one copy for the
-// whole tile when its rows are adjacent) into a dense [row][element] stage,
-// which the element-fastest thread mapping reads without bank conflicts for
-// L >= 256.  The Stockham exchanges then use the padded per-row layout of
-// k_pass in the same stage, and the outputs are staged densely again for
-// bulk copies out.  A partial last tile copies only its rows.
+// whole tile when its rows are adjacent and unpadded) into a [row][element]
+// stage of row stride RS, read with the element-fastest thread mapping
+// (thread t of a row holds elements t + m TF).  For L >= 256 a half-warp
+// reads within one row and RS = L (dense); shorter rows put 16 / TF rows in a
+// half-warp, and RS = L + TF (= TF mod 16, 16-byte aligned) spreads them over
+// all banks.  The Stockham exchanges then use a padded per-row layout in the
+// same stage, and the outputs are staged with row stride RS again for bulk
+// copies out.  A partial last tile copies only its rows.
 template <int LOG2L>
 struct PassRGeo {
     static constexpr int L = 1 << LOG2L;
@@ -313,13 +316,16 @@ struct PassRGeo {
     static constexpr int TF = L / E;
     static constexpr int K = 256 / TF;  // 256 threads
     static constexpr int THREADS = 256;
-    static constexpr int LPAD = (L + (L >> 4)) | 1;
+    static constexpr int RS = L >= 256 ? L : L + TF;
+    // exchange row stride: odd for L >= 256; = TF mod 16 below (L + L/16)
+    static constexpr int LPAD = L >= 256 ? (L + (L >> 4)) | 1 : L + (L >> 4);
+    static constexpr int ROWW = RS > LPAD ? RS : LPAD;
     // bulk copies need 16-byte alignment only: 128-byte rounding, not 1 KB
-    static constexpr int SB = ((K * LPAD * 8) + 127) / 128 * 128;
+    static constexpr int SB = ((K * ROWW * 8) + 127) / 128 * 128;
     static constexpr int STAGES = 2;
     static constexpr int MINB = 3;
     static constexpr size_t SMEM = 128 + (size_t)STAGES * SB + 64 + (size_t)tw_total(LOG2L) * sizeof(float2);
-    static_assert(L >= 256 && K >= 1, "row tiles need L >= 256");
+    static_assert(L >= 32 && K >= 1 && (RS * 8) % 16 == 0, "row tile geometry");
 };
 
 template <int LOG2L>
@@ -362,21 +368,28 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
     }
     __syncthreads();
 
-    auto issue = [&](int64_t tl, int s) {  // thread 0 only
+    // Called by every thread for L < 256, else by thread 0.  Thread 0 posts the tile's byte count; the row
+    // copies are spread over threads tid < K when there are many (L < 256) --
+    // a copy may complete before the count is posted, the phase cannot (its
+    // one arrival is thread 0's).
+    auto issue = [&](int64_t tl, int s) {
         const int64_t f0 = tl * G::K;
         const int rows = static_cast<int>(a.nsub - f0 < G::K ? a.nsub - f0 : G::K);
         float2* dst = stage(s);
         const uint32_t row_bytes = static_cast<uint32_t>(G::L * sizeof(float2));
-        mbar_arrive_expect_tx(&full[s], row_bytes * rows);
+        if (tid == 0) mbar_arrive_expect_tx(&full[s], row_bytes * rows);
         if (in_contig) {
-            bulk_load(dst, row_in(f0), row_bytes * rows, &full[s]);
+            if (tid == 0) bulk_load(dst, row_in(f0), row_bytes * rows, &full[s]);
+        } else if constexpr (G::L >= 256) {
+            if (tid == 0)
+                for (int r = 0; r < rows; ++r) bulk_load(dst + r * G::RS, row_in(f0 + r), row_bytes, &full[s]);
         } else {
-            for (int r = 0; r < rows; ++r) bulk_load(dst + r * G::L, row_in(f0 + r), row_bytes, &full[s]);
+            if (tid < rows) bulk_load(dst + tid * G::RS, row_in(f0 + tid), row_bytes, &full[s]);
         }
     };
 
     int64_t tile = blockIdx.x;
-    if (tid == 0 && tile < ntiles) issue(tile, 0);
+    if ((G::L < 256 || tid == 0) && tile < ntiles) issue(tile, 0);
     int it = 0;
     bool aborted = false;
     for (; tile < ntiles; ++it, tile += gridDim.x) {
@@ -393,7 +406,7 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
 #pragma unroll
         for (int m = 0; m < 16; ++m) {
             const uint32_t e = static_cast<uint32_t>(t + m * G::TF);
-            float2 val = ok ? buf[cl * G::L + e] : make_float2(0.f, 0.f);
+            float2 val = ok ? buf[cl * G::RS + e] : make_float2(0.f, 0.f);
             if (a.conj_in) val.y = -val.y;
             if (a.tw_mode == 1) val = cmul(val, twiddle(e * cmul32));
             v[m] = val;
@@ -402,7 +415,7 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
             aborted = true;
             break;
         }
-        if (tid == 0 && tile + gridDim.x < ntiles) issue(tile + gridDim.x, (it + 1) % G::STAGES);
+        if ((G::L < 256 || tid == 0) && tile + gridDim.x < ntiles) issue(tile + gridDim.x, (it + 1) % G::STAGES);
 
         // packed FP32x2 adds: +7-9 % on these passes (measured; not on the column pass)
         stockham_passes<LOG2L, 0, 16, G::TF, 0, true>(v, t, buf + cl * G::LPAD, tw_smem);
@@ -412,7 +425,7 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
             const uint32_t k = static_cast<uint32_t>(t + m * G::TF);
             float2 val = v[m];
             if (a.tw_mode == 2) val = cmul(val, twiddle(k * cmul32));
-            buf[cl * G::L + k] = scaled ? make_float2(val.x * osr, val.y * osi) : val;
+            buf[cl * G::RS + k] = scaled ? make_float2(val.x * osr, val.y * osi) : val;
         }
         fence_proxy_async_smem();
         __syncthreads();
@@ -425,7 +438,7 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
                 bulk_commit();
             }
         } else if (tid < G::K) {
-            if (tid < rows) bulk_store(row_out(f0 + tid), buf + tid * G::L, row_bytes);
+            if (tid < rows) bulk_store(row_out(f0 + tid), buf + tid * G::RS, row_bytes);
             bulk_commit();  // an empty group keeps every storing thread's group count in step
         }
         (void)active;
@@ -542,7 +555,8 @@ static cudaError_t launch_pass_tma_rows_t(const float2* in, float2* out, const P
 // Row tiles through bulk copies when the shapes allow it.
 static cudaError_t launch_pass_tma_rows(int log2l, const float2* in, float2* out, const PassArgs& a,
                                         cudaStream_t s) {
-    if (log2l < 8 || log2l > 12) return cudaErrorNotSupported;
+    // 16-point rows (one thread per row, 256 copies per tile) measured faster on k_pass
+    if (log2l < 5 || log2l > 12) return cudaErrorNotSupported;
     const int64_t L = int64_t(1) << log2l;
     const int k = 256 / (int)(L / 16);
     const int64_t inner = int64_t(1) << a.inner_log2;
@@ -557,9 +571,13 @@ static cudaError_t launch_pass_tma_rows(int log2l, const float2* in, float2* out
         if (inner == 1) return outer == L;
         return !base_bits && inner_stride == L && outer == inner * L && inner % k == 0;
     };
-    const int in_contig = contiguous(a.in_outer, a.in_inner, a.in_base_bits) ? 1 : 0;
-    const int out_contig = contiguous(a.out_outer, a.out_inner, a.out_base_bits) ? 1 : 0;
+    // padded stages (L < 256) take one copy per row
+    const int in_contig = log2l >= 8 && contiguous(a.in_outer, a.in_inner, a.in_base_bits) ? 1 : 0;
+    const int out_contig = log2l >= 8 && contiguous(a.out_outer, a.out_inner, a.out_base_bits) ? 1 : 0;
     switch (log2l) {
+        case 5: return launch_pass_tma_rows_t<5>(in, out, a, in_contig, out_contig, s);
+        case 6: return launch_pass_tma_rows_t<6>(in, out, a, in_contig, out_contig, s);
+        case 7: return launch_pass_tma_rows_t<7>(in, out, a, in_contig, out_contig, s);
         case 8: return launch_pass_tma_rows_t<8>(in, out, a, in_contig, out_contig, s);
         case 9: return launch_pass_tma_rows_t<9>(in, out, a, in_contig, out_contig, s);
         case 10: return launch_pass_tma_rows_t<10>(in, out, a, in_contig, out_contig, s);

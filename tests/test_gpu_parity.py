@@ -399,12 +399,14 @@ def test_installed_b200_table_selects_and_executes():
         assert rel_l2_per_transform(y, ref) <= TOL_F64, (n, b, tt, p.executed)
 
 
-@pytest.mark.parametrize("n, tiles", [(256, (256,)), (1024, (1024,)), (4096, (4096,)), (8192, (256, 512)),
+@pytest.mark.parametrize("n, tiles", [(16, (16,)), (32, (32,)), (64, (64,)), (128, (128,)), (256, (256,)),
+                                      (1024, (1024,)), (4096, (4096,)), (8192, (256, 512)),
                                       (65536, (256,)), (1 << 18, (64, 512))])
 def test_tma_passes_odd_batches(n, tiles):
     """The bulk-copy row pass (partial last tiles when B is not a multiple of
-    the rows per tile) and the TMA column pass (every tail pass, strided local
-    groups), both directions, forward and ortho inverse."""
+    the rows per tile; padded per-row copies below 256 points) and the TMA
+    column pass (every tail pass, strided local groups), both directions,
+    forward and ortho inverse."""
     rng = np.random.default_rng(n)
     for b in (1, 2, 8):  # the runner functions take power-of-two batches (the reference's rule)
         x = cplx(rng, (b, n))
