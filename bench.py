@@ -310,7 +310,10 @@ class Ctx:
         """(max-over-ranks ms of `steps` calls of fn, launches, clocks).
 
         flush_l2: inputs smaller than L2 -- before every step a 256 MiB buffer
-        is written (outside the timed spans) and only the call is timed."""
+        is written (outside the timed spans) and only the call is timed; a
+        device-side spin after the flush keeps the GPU busy while the host
+        enqueues the call, so the span holds the device work, not the host's
+        launch overhead."""
         from bfft import _lib
 
         torch = self.torch
@@ -331,6 +334,7 @@ class Ctx:
                 spans = []
                 for _ in range(steps):
                     flush.fill_(1)
+                    torch.cuda._sleep(400_000)  # ~0.2 ms at B200 clocks, longer than one call's enqueue
                     a = torch.cuda.Event(enable_timing=True)
                     b = torch.cuda.Event(enable_timing=True)
                     a.record(self.stream)

@@ -170,14 +170,24 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
     const float osr = a.scale, osi = a.conj_out ? -a.scale : a.scale;
     const bool scaled = a.scale != 1.0f || a.conj_out;  // uniform: skip the epilogue multiply when it is 1
 
-    fill_stockham_twiddles<LOG2L>(tw_smem);
-    SmemTwiddle<TW3 ? 3 : 2> twiddle;  // W_N lookups, staged in shared memory when they fit
-    twiddle.setup(coltw + G::COLTW_ENTRIES, a);
-    if (tid == 0) {
+    auto issue = [&](int64_t tl, int s) {  // thread 0 only
+        const int64_t f0 = tl * G::K;
+        const int o = static_cast<int>(f0 >> a.inner_log2), c0 = static_cast<int>(f0 & imask);
+        float2* dst = stage(s);
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(G::K * G::L * sizeof(float2)));
+#pragma unroll
+        for (int j = 0; j < G::L / G::LB; ++j) tma_load_3d(dst + j * G::LB * G::K, &tin, c0, j * G::LB, o, &full[s]);
+    };
+    int64_t tile = blockIdx.x;
+    if (tid == 0) {  // the first tile is in flight while the tables are filled
         for (int s = 0; s < G::STAGES; ++s) mbar_init(&full[s], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_proxy_async_smem();
+        if (tile < ntiles) issue(tile, 0);
     }
+    fill_stockham_twiddles<LOG2L>(tw_smem);
+    SmemTwiddle<TW3 ? 3 : 2> twiddle;  // W_N lookups, staged in shared memory when they fit
+    twiddle.setup(coltw + G::COLTW_ENTRIES, a);
     __syncthreads();
 
     // The W_N twiddle of element e = t + m TF of sub-FFT c is W^{e C} with
@@ -195,17 +205,6 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
     // rev(t) * 16 + rev4(m): a per-thread base plus a constant per element
     const uint32_t rt16 = LOG2L > 4 ? (brev_bits(static_cast<uint32_t>(t), LOG2L - 4) << 4) : 0u;
 
-    auto issue = [&](int64_t tl, int s) {  // thread 0 only
-        const int64_t f0 = tl * G::K;
-        const int o = static_cast<int>(f0 >> a.inner_log2), c0 = static_cast<int>(f0 & imask);
-        float2* dst = stage(s);
-        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(G::K * G::L * sizeof(float2)));
-#pragma unroll
-        for (int j = 0; j < G::L / G::LB; ++j) tma_load_3d(dst + j * G::LB * G::K, &tin, c0, j * G::LB, o, &full[s]);
-    };
-
-    int64_t tile = blockIdx.x;
-    if (tid == 0 && tile < ntiles) issue(tile, 0);
     int it = 0;
     bool aborted = false;
     for (; tile < ntiles; ++it, tile += gridDim.x) {
@@ -348,9 +347,6 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
     const bool scaled = a.scale != 1.0f || a.conj_out;  // uniform: skip the epilogue multiply when it is 1
     const int NST = out_contig ? 1 : G::K;  // threads that issue (and wait for) stores
 
-    fill_stockham_twiddles<LOG2L>(tw_smem);
-    SmemTwiddle<2> twiddle;  // W_N lookups, staged in shared memory when they fit
-    twiddle.setup(tw_smem + tw_total(LOG2L), a);
     auto row_in = [&](int64_t f) -> const float2* {
         const int64_t o = f >> a.inner_log2, c = f & imask;
         const int64_t cin = a.in_base_bits ? (int64_t)brev_bits((uint32_t)c, a.in_base_bits) : c;
@@ -361,17 +357,10 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
         const int64_t cout = a.out_base_bits ? (int64_t)brev_bits((uint32_t)c, a.out_base_bits) : c;
         return out + o * a.out_outer + cout * a.out_inner;
     };
-    if (tid == 0) {
-        for (int s = 0; s < G::STAGES; ++s) mbar_init(&full[s], 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        fence_proxy_async_smem();
-    }
-    __syncthreads();
-
-    // Called by every thread for L < 256, else by thread 0.  Thread 0 posts the tile's byte count; the row
-    // copies are spread over threads tid < K when there are many (L < 256) --
-    // a copy may complete before the count is posted, the phase cannot (its
-    // one arrival is thread 0's).
+    // Called by every thread for L < 256, else by thread 0.  Thread 0 posts
+    // the tile's byte count; the row copies are spread over threads tid < K
+    // when there are many (L < 256) -- a copy may complete before the count
+    // is posted, the phase cannot (its one arrival is thread 0's).
     auto issue = [&](int64_t tl, int s) {
         const int64_t f0 = tl * G::K;
         const int rows = static_cast<int>(a.nsub - f0 < G::K ? a.nsub - f0 : G::K);
@@ -389,7 +378,18 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
     };
 
     int64_t tile = blockIdx.x;
-    if ((G::L < 256 || tid == 0) && tile < ntiles) issue(tile, 0);
+    if (tid == 0) {
+        for (int s = 0; s < G::STAGES; ++s) mbar_init(&full[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_proxy_async_smem();
+        // one issuing thread: the first tile is in flight while the tables are filled
+        if (G::L >= 256 && tile < ntiles) issue(tile, 0);
+    }
+    fill_stockham_twiddles<LOG2L>(tw_smem);
+    SmemTwiddle<2> twiddle;  // W_N lookups, staged in shared memory when they fit
+    twiddle.setup(tw_smem + tw_total(LOG2L), a);
+    __syncthreads();
+    if (G::L < 256 && tile < ntiles) issue(tile, 0);  // the barriers are initialised now
     int it = 0;
     bool aborted = false;
     for (; tile < ntiles; ++it, tile += gridDim.x) {
