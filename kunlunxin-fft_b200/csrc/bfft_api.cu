@@ -523,12 +523,18 @@ void set_last_epilogue(std::vector<Step>& st, int conj, float scale) {
     }
 }
 
-cudaError_t launch_step(const Step& s, const float2* in, float2* out, cudaStream_t stream) {
+// after_pass: the previous kernel on the stream is a pass of this flow, so a
+// TMA pass may be launched as its programmatic dependent.
+cudaError_t launch_step(const Step& s, const float2* in, float2* out, cudaStream_t stream, bool after_pass = false) {
     g_launches.fetch_add(1, std::memory_order_relaxed);
     switch (s.kind) {
         case S_STAGE2: return launch_radix2_stage(s.dif, in, out, s.st, s.block, stream);
         case S_STAGE4: return launch_radix4_stage(s.dif, in, out, s.st, s.block, stream);
-        case S_PASS: return launch_pass(s.log2l, s.layout, s.lmap, s.smap, in, out, s.pa, stream);
+        case S_PASS: {
+            PassArgs pa = s.pa;
+            pa.pdl = after_pass ? 1 : 0;
+            return launch_pass(s.log2l, s.layout, s.lmap, s.smap, in, out, pa, stream);
+        }
         case S_CLUSTER: return launch_cluster_fft(s.log2l, in, out, s.ca, stream);
         default: return cudaErrorInvalidValue;
     }
@@ -542,7 +548,7 @@ cudaError_t run_core(const std::vector<Step>& st, const float2* src, float2* dst
     const float2* cur = src;
     for (size_t i = 0; i < L; ++i) {
         float2* tgt = ((L - 1 - i) % 2 == 0) ? dst : scratch;
-        cudaError_t e = launch_step(st[i], cur, tgt, stream);
+        cudaError_t e = launch_step(st[i], cur, tgt, stream, i > 0 && st[i - 1].kind == S_PASS);
         if (e != cudaSuccess) return e;
         cur = tgt;
     }
@@ -637,9 +643,10 @@ bfft_status bfft_plan_create(const bfft_plan_desc* desc, bfft_plan_t* plan) {
         P->ws_bytes = L > 1 ? cbytes : 0;
         P->launches = L == 0 ? 1 : L;
     } else if (dedicated) {
-        // r2c: core (in -> F via A) + stitch; c2r: pre (in -> C) + core (C -> F via A) + unpack
+        // r2c: core (in -> F via A) + stitch; c2r: pre (in -> C) + core (C -> out via A,
+        // the unpack fused; a one-point core keeps the scale + unpack kernels)
         P->ws_bytes = (d.transform_type == BFFT_R2C ? 2 : 3) * cbytes;
-        P->launches = (L == 0 ? 1 : L) + (d.transform_type == BFFT_R2C ? 1 : 2);
+        P->launches = d.transform_type == BFFT_R2C ? (L == 0 ? 1 : L) + 1 : (L == 0 ? 3 : L + 1);
     } else {
         P->ws_bytes = 3 * sizeof(float2) * (size_t)(B * n);
         P->launches = (L == 0 ? 1 : L) + 2;
@@ -719,13 +726,18 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
             const float scale = (float)(2.0 * norm_scale(n, BFFT_INVERSE, d.norm));
             g_launches.fetch_add(1, std::memory_order_relaxed);
             e = launch_c2r_pre((const float2*)in, C, n, B, plan->twf.tw, s);
-            if (e == cudaSuccess) {
-                e = core.empty() ? launch_scale(C, F, B * c, 1.0f, 0, s) : run_core(core, C, F, A, s);
-                if (core.empty()) g_launches.fetch_add(1, std::memory_order_relaxed);
-            }
-            if (e == cudaSuccess) {
-                g_launches.fetch_add(1, std::memory_order_relaxed);
-                e = launch_c2r_unpack(F, (float*)out, n, B, scale, s);
+            if (e == cudaSuccess && !core.empty()) {
+                // The reference's unpack reads the core DFT reversed, u[(N/2 - k) mod N/2]
+                // = conj(DFT(conj z))[k]: with the conjugates and the scale fused into
+                // the first and last pass, the core writes the real output itself
+                // (float32 pairs = complex64 (B, N/2)) and the unpack pass goes away.
+                set_first_conj(core);
+                set_last_epilogue(core, 1, scale);
+                e = run_core(core, C, (float2*)out, A, s);
+            } else if (e == cudaSuccess) {
+                g_launches.fetch_add(2, std::memory_order_relaxed);
+                e = launch_scale(C, F, B * c, 1.0f, 0, s);
+                if (e == cudaSuccess) e = launch_c2r_unpack(F, (float*)out, n, B, scale, s);
             }
         }
     } else {

@@ -112,6 +112,10 @@ struct PassArgs {
     const float2* unit_tw;  // unit twiddle levels (ensure_unit_twiddles)
     int tw_smem_entries;    // set by launch_pass: shared-memory entries of the staged W_N tables
     int tw_smem_levels;     // set by launch_pass: 0 global two-level, 2 / 3 staged two- / three-level
+    // 1: the previous kernel on the stream is a pass of the same flow -- a TMA
+    // pass is then launched as its programmatic dependent (it may start while
+    // that kernel drains and waits for it before touching its output)
+    int pdl;
 };
 
 constexpr int kMaxPassLog2 = 12;  // largest CTA-resident sub-FFT: 4096 points

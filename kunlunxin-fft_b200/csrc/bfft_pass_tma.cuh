@@ -111,6 +111,17 @@ template <int N>
 __device__ __forceinline__ void bulk_wait() {
     asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
+// Programmatic dependent launch: launch_dependents lets the next kernel on
+// the stream (if launched as a programmatic dependent) be scheduled once
+// every CTA of this grid has issued it or exited -- its CTAs then take the
+// SMs this grid's finished CTAs free and fill their tables; griddep_wait
+// blocks until the previous kernel has completed and its writes are visible
+// (at once for an ordinary launch).
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Generic-proxy writes to shared memory become visible to the async proxy
 // (the TMA store engine) after this fence and a barrier.
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -179,10 +190,12 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
         for (int j = 0; j < G::L / G::LB; ++j) tma_load_3d(dst + j * G::LB * G::K, &tin, c0, j * G::LB, o, &full[s]);
     };
     int64_t tile = blockIdx.x;
+    if (tile >= ntiles) griddep_launch_dependents();  // no tile for this CTA
     if (tid == 0) {  // the first tile is in flight while the tables are filled
         for (int s = 0; s < G::STAGES; ++s) mbar_init(&full[s], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_proxy_async_smem();
+        griddep_wait();  // every read and write of the flow's buffers follows this (tables are plan-owned)
         if (tile < ntiles) issue(tile, 0);
     }
     fill_stockham_twiddles<LOG2L>(tw_smem);
@@ -208,6 +221,10 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
     int it = 0;
     bool aborted = false;
     for (; tile < ntiles; ++it, tile += gridDim.x) {
+        // the next pass may be scheduled once every CTA is on its last tile
+        // (measured: as fast as triggering at the start on short flows, no
+        // interference with long ones)
+        if (tile + gridDim.x >= ntiles) griddep_launch_dependents();
         const int s = it % G::STAGES;
         float2* buf = stage(s);
         const int64_t f = tile * G::K + cl;
@@ -378,10 +395,12 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
     };
 
     int64_t tile = blockIdx.x;
+    if (tile >= ntiles) griddep_launch_dependents();  // no tile for this CTA
     if (tid == 0) {
         for (int s = 0; s < G::STAGES; ++s) mbar_init(&full[s], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_proxy_async_smem();
+        griddep_wait();  // every read and write of the flow's buffers follows this (tables are plan-owned)
         // one issuing thread: the first tile is in flight while the tables are filled
         if (G::L >= 256 && tile < ntiles) issue(tile, 0);
     }
@@ -393,6 +412,10 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
     int it = 0;
     bool aborted = false;
     for (; tile < ntiles; ++it, tile += gridDim.x) {
+        // the next pass may be scheduled once every CTA is on its last tile
+        // (measured: as fast as triggering at the start on short flows, no
+        // interference with long ones)
+        if (tile + gridDim.x >= ntiles) griddep_launch_dependents();
         const int s = it % G::STAGES;
         float2* buf = stage(s);
         const int64_t f = tile * G::K + cl;
@@ -449,6 +472,28 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
 }
 
 // ---- host side ----
+
+// An ordinary launch, or (pdl) one with programmatic stream serialisation.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_maybe_pdl(void (*kern)(KArgs...), unsigned grid, unsigned threads, size_t smem,
+                                    cudaStream_t s, int pdl, Args... args) {
+    if (!pdl) {
+        kern<<<grid, threads, smem, s>>>(args...);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
 
 using EncodeTiledFn = PFN_cuTensorMapEncodeTiled_v12000;
 
@@ -518,10 +563,10 @@ static cudaError_t launch_pass_tma_t(const float2* in, float2* out, const PassAr
     if (grid < 1) grid = 1;
     const size_t smem = G::SMEM + (size_t)b.tw_smem_entries * sizeof(float2);
     if (tw3)
-        k_pass_tma<LOG2L, ROWS, true><<<(unsigned)grid, G::THREADS, smem, s>>>(tin, tout, out, b);
-    else
-        k_pass_tma<LOG2L, ROWS, false><<<(unsigned)grid, G::THREADS, smem, s>>>(tin, tout, out, b);
-    return cudaGetLastError();
+        return launch_maybe_pdl(k_pass_tma<LOG2L, ROWS, true>, (unsigned)grid, G::THREADS, smem, s, b.pdl, tin, tout,
+                                out, b);
+    return launch_maybe_pdl(k_pass_tma<LOG2L, ROWS, false>, (unsigned)grid, G::THREADS, smem, s, b.pdl, tin, tout,
+                            out, b);
 }
 
 template <int LOG2L>
@@ -548,8 +593,7 @@ static cudaError_t launch_pass_tma_rows_t(const float2* in, float2* out, const P
     if (grid > ntiles) grid = ntiles;
     if (grid < 1) grid = 1;
     const size_t smem = G::SMEM + (size_t)b.tw_smem_entries * sizeof(float2);
-    kern<<<(unsigned)grid, G::THREADS, smem, s>>>(in, out, b, in_contig, out_contig);
-    return cudaGetLastError();
+    return launch_maybe_pdl(kern, (unsigned)grid, G::THREADS, smem, s, b.pdl, in, out, b, in_contig, out_contig);
 }
 
 // Row tiles through bulk copies when the shapes allow it.
