@@ -1,4 +1,5 @@
-"""Collected last: no kernel of the GPU tests gave up a bounded wait (the TMA
+"""Collected after every parity test (only the allocation-free entry point's
+file comes later): no kernel of the GPU tests gave up a bounded wait (the TMA
 pass records an expired mbarrier wait in the device status word)."""
 import pytest
 
