@@ -430,6 +430,27 @@ def test_tma_passes_odd_batches(n, tiles):
     assert _lib.device_status(0) == 0
 
 
+@pytest.mark.parametrize("n, b, tile", [(64, 64, 64), (1024, 8, 1024), (65536, 4, 256), (1 << 18, 2, 512)])
+def test_unaligned_buffers_take_the_fallback_pass(n, b, tile):
+    """Input, output and workspace 8 but not 16 bytes aligned: the TMA column
+    pass and the bulk-copy row pass need 16-byte aligned buffers, so the
+    library runs these passes on its cp.async pass instead -- the results are
+    as accurate as from aligned buffers."""
+    rng = np.random.default_rng(n + b)
+    x = cplx(rng, (b, n))
+    plan = runner.native_plan("fft_dit_matrix_batch", "dit", n, b, 0, tile=tile, block=256)
+    xin = torch.empty(b * n + 1, dtype=torch.complex64, device=DEV)
+    xin[1:].copy_(torch.from_numpy(x).reshape(-1))
+    out = torch.zeros(b * n + 1, dtype=torch.complex64, device=DEV)
+    ws = torch.empty(plan.workspace_bytes + 8, dtype=torch.uint8, device=DEV) if plan.workspace_bytes else None
+    assert xin[1:].data_ptr() % 16 == 8 and out[1:].data_ptr() % 16 == 8
+    plan.execute(xin[1:].data_ptr(), out[1:].data_ptr(), ws.data_ptr() + 8 if ws is not None else 0,
+                 plan.workspace_bytes, torch.cuda.current_stream(DEV).cuda_stream)
+    y = host(out[1:]).reshape(b, n)
+    assert rel_l2_per_transform(y, _f64(x)) <= TOL_F64, (n, b, tile)
+    assert _lib.device_status(0) == 0
+
+
 @pytest.mark.parametrize("n, b, tt, chunks", [(1024, 64, "c2c", 4), (65536, 32, "c2c", 8), (4096, 16, "r2c", 4),
                                              (4096, 16, "c2r", 2), (2048, 1, "c2c", 1)])
 def test_host_buffer_execution(n, b, tt, chunks):
