@@ -50,7 +50,7 @@ WORKLOADS = {
     "c4-c2r": {"n": 65536, "batch": 256, "tt": "c2r", "td": "inverse",
                "desc": "config 4: C2R inverse, N=65536, B=256 (half spectrum in, float32 out)"},
     "5b": {"n": 1 << 30, "batch": 1, "kind": "4step", "cpu_n": 1 << 20,
-           "desc": "config 5b: one C2C forward of N=2^30 (8 GiB complex64); 4-step over ranks with NCCL all-to-all"},
+           "desc": "config 5b: one C2C forward of N=2^30 (8 GiB complex64); distributed 4-step over ranks (exchanges fused with the transposes, or NCCL all-to-all)"},
 }
 SEED = 1234
 # DRAM bytes per launch of the dominant kernel, from an ncu capture of a small
