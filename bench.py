@@ -499,7 +499,7 @@ def run_4step(args, wl, ctx) -> dict:
         native = native_plan_for(plan, ctx.local)
         per_launch_ms = ms_step / max(native.launches, 1)
         bpl = 16.0 * n
-        roofline = {"bound": "hbm", "kernel": "k_pass (CTA-resident Stockham pass)",
+        roofline = {"bound": "hbm", "kernel": "k_pass_tma (TMA column pass; CTA-resident Stockham)",
                     "achieved": bpl / (per_launch_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                     "peak_source": peak_src, "traffic": None, "launches_per_step": native.launches,
                     "algorithmic_bytes_per_launch": bpl, "transform_hbm_gbs": 16.0 * n / (ms_step / 1e3) / 1e9}
