@@ -962,13 +962,72 @@ cudaError_t read_device_status(unsigned* status, bool clear) {
     return e;
 }
 
+// ---- rows of 2 points: one row per thread, in registers ----
+//
+// A 2-point row is one 16-byte vector: each thread loads its row, runs the
+// butterfly in registers and stores it -- a warp reads and writes 512
+// contiguous bytes, no shared memory, no barriers.  (The same kernel for 4..16
+// points, each row a few 16-byte loads of one thread, measured 0-22 % slower
+// than the k_pass row tile: a warp's loads touch 32 lines at a time.)
+template <int LOG2L>
+__global__ void __launch_bounds__(256) k_rows_regs(const float2* __restrict__ in, float2* __restrict__ out,
+                                                   PassArgs a) {
+    constexpr int L = 1 << LOG2L;
+    const int64_t imask = (int64_t(1) << a.inner_log2) - 1;
+    const float osr = a.scale, osi = a.conj_out ? -a.scale : a.scale;
+    const bool scaled = a.scale != 1.0f || a.conj_out;
+    for (int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; f < a.nsub;
+         f += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t o = f >> a.inner_log2, c = f & imask;
+        const int64_t cin = a.in_base_bits ? (int64_t)brev_bits((uint32_t)c, a.in_base_bits) : c;
+        const int64_t cout = a.out_base_bits ? (int64_t)brev_bits((uint32_t)c, a.out_base_bits) : c;
+        const float4* src = reinterpret_cast<const float4*>(in + o * a.in_outer + cin * a.in_inner);
+        float4* dst = reinterpret_cast<float4*>(out + o * a.out_outer + cout * a.out_inner);
+        float2 v[L];
+#pragma unroll
+        for (int j = 0; j < L / 2; ++j) {
+            const float4 q = __ldg(src + j);
+            v[2 * j] = make_float2(q.x, a.conj_in ? -q.y : q.y);
+            v[2 * j + 1] = make_float2(q.z, a.conj_in ? -q.w : q.w);
+        }
+        Dft<L, true>::run(v);
+        if (scaled) {
+#pragma unroll
+            for (int m = 0; m < L; ++m) v[m] = make_float2(v[m].x * osr, v[m].y * osi);
+        }
+#pragma unroll
+        for (int j = 0; j < L / 2; ++j) __stcs(dst + j, make_float4(v[2 * j].x, v[2 * j].y, v[2 * j + 1].x, v[2 * j + 1].y));
+    }
+}
+
+template <int LOG2L>
+static cudaError_t launch_rows_regs_t(const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
+    k_rows_regs<LOG2L><<<flat_grid(a.nsub, 256), 256, 0, s>>>(in, out, a);
+    return cudaGetLastError();
+}
+
+// The register-only row kernel when the shape allows it (rows of 2
+// contiguous points, every row start 16-byte aligned, no W_N twiddle).
+static cudaError_t launch_rows_regs(int log2l, const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
+    if (log2l != 1) return cudaErrorNotSupported;
+    const int64_t inner = int64_t(1) << a.inner_log2;
+    if (((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) || a.in_stride != 1 ||
+        a.out_stride != 1 || a.in_elem_bitrev || a.out_elem_bitrev || a.tw_mode != 0)
+        return cudaErrorNotSupported;
+    if ((a.in_outer & 1) || (inner > 1 && (a.in_inner & 1)) || (a.out_outer & 1) || (inner > 1 && (a.out_inner & 1)))
+        return cudaErrorNotSupported;
+    return launch_rows_regs_t<1>(in, out, a, s);
+}
+
 cudaError_t launch_pass(int log2l, int layout, int lmap, int smap, const float2* in, float2* out,
                         const PassArgs& a, cudaStream_t s) {
     if (layout == 1) {  // column tiles: TMA-staged pass when the shape allows it
         const cudaError_t e = launch_pass_tma(log2l, in, out, a, s);
         if (e != cudaErrorNotSupported) return e;
     } else if (smap != 2) {  // row tiles with row outputs: bulk-copy pass when the shape allows it
-        const cudaError_t e = launch_pass_tma_rows(log2l, in, out, a, s);
+        cudaError_t e = launch_rows_regs(log2l, in, out, a, s);
+        if (e != cudaErrorNotSupported) return e;
+        e = launch_pass_tma_rows(log2l, in, out, a, s);
         if (e != cudaErrorNotSupported) return e;
     }
     switch (log2l) {
