@@ -1006,80 +1006,98 @@ static cudaError_t launch_rows_regs_t(const float2* in, float2* out, const PassA
     return cudaGetLastError();
 }
 
-// ---- contiguous rows of 16 points: a warp per 32 rows, exchanges by shuffles ----
+// ---- adjacent short rows (L = 16..64 points): shuffles instead of shared memory ----
 //
-// The warp reads its 32 rows (4 KB) with fully coalesced 16-byte loads: in
-// load j, lane l holds elements 2i, 2i+1 (i = l mod 8) of row 4j + l/8.  A
-// 16-point DFT is X[k1 + 8 k2] = Y0[k1] + (-1)^k2 W16^k1 Y1[k1] with Ys the
-// 8-point DFT of the elements 2i + s, which the row's 8 lanes compute
-// together: three radix-2 decimation-in-frequency steps across lanes
-// (shfl_xor 4, 2, 1), after which lane i holds Ys[bitrev3(i)].  No shared
-// memory, no barriers.
-__global__ void __launch_bounds__(256) k_rows16_shfl(const float2* __restrict__ in, float2* __restrict__ out,
-                                                     int64_t nrows, int conj_in, int conj_out, float scale) {
-    const int lane = threadIdx.x & 31, i = lane & 7;
-    const int k1 = ((i & 1) << 2) | (i & 2) | ((i & 4) >> 2);  // bitrev3(i)
-    const float2 w4 = g_tw_levels[8 + (i & 3)];                 // W8^(i mod 4), upper half of step 1
-    const float2 w2 = g_tw_levels[4 + (i & 1)];                 // W4^(i mod 2), upper half of step 2
-    const float2 w16 = g_tw_levels[16 + k1];                    // W16^k1
+// G = L/2 lanes share a row, each holding two consecutive elements (one
+// 16-byte vector), so a warp's eight fully coalesced 16-byte loads cover
+// 8 * 32/G adjacent rows: in load j, lane l holds elements 2i, 2i+1
+// (i = l mod G) of row 8 (32/G) g + j (32/G) + l/G.  An L-point DFT is
+// X[k1 + (L/2) k2] = Y0[k1] + (-1)^k2 W_L^k1 Y1[k1] with Ys the (L/2)-point
+// DFT of the elements 2i + s; the row's G lanes compute both with log2 G
+// radix-2 decimation-in-frequency steps across lanes (shfl_xor G/2 .. 1),
+// after which lane i holds Ys[bitrev(i)].  All eight loads are in flight
+// before the first shuffle; no shared memory, no barriers.  Measured against
+// the shared-memory row passes on B*N = 2^24: 16 points 63.5 -> 51.5 µs,
+// 32 points 59.5 -> 51.2, 64 points 57.0 -> 55.0; for 4 and 8 points the
+// k_pass row tile is as fast or faster.
+template <int LOG2L>
+__global__ void __launch_bounds__(256) k_rows_shfl(const float2* __restrict__ in, float2* __restrict__ out,
+                                                   int64_t nrows, int conj_in, int conj_out, float scale) {
+    constexpr int L = 1 << LOG2L, G = L / 2, LG = LOG2L - 1, RPL = 32 / G;  // rows per load
+    const int lane = threadIdx.x & 31, i = lane & (G - 1);
+    const int k1 = LG ? (int)(__brev((unsigned)i) >> (32 - LG)) : 0;
+    float2 wstep[LG > 0 ? LG : 1];  // step q (h = G >> (q + 1)): W_{2h}^(i mod h)
+#pragma unroll
+    for (int q = 0; q < LG; ++q) {
+        const int h = G >> (q + 1);
+        wstep[q] = g_tw_levels[2 * h + (i & (h - 1))];
+    }
+    const float2 wl = g_tw_levels[L + k1];  // W_L^k1
     const float osr = scale, osi = conj_out ? -scale : scale;
-    const int64_t groups = (nrows + 31) >> 5;
+    const int64_t groups = (nrows + 8 * RPL - 1) / (8 * RPL);
     const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    auto xstep = [&](float2 v, int h, float2 w) {  // one radix-2 DIF step across the lanes i and i ^ h
-        const float2 p = make_float2(__shfl_xor_sync(0xffffffffu, v.x, h, 8), __shfl_xor_sync(0xffffffffu, v.y, h, 8));
-        return (i & h) ? cmul(csub(p, v), w) : cadd(v, p);
-    };
     for (int64_t g = warp; g < groups; g += nwarps) {
-        const int64_t r0 = g << 5;
-        const float4* src = reinterpret_cast<const float4*>(in + r0 * 16);
-        float4 q[8];  // all eight loads in flight before the first shuffle
+        const int64_t r0 = g * 8 * RPL;
+        const float4* src = reinterpret_cast<const float4*>(in + r0 * L);
+        float4 q[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-            q[j] = r0 + 4 * j + (lane >> 3) < nrows ? __ldcs(src + lane + 32 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            q[j] = r0 + j * RPL + lane / G < nrows ? __ldcs(src + lane + 32 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int64_t row = r0 + 4 * j + (lane >> 3);
-            const bool live = row < nrows;
-            float2 y0 = make_float2(q[j].x, conj_in ? -q[j].y : q[j].y);
-            float2 y1 = make_float2(q[j].z, conj_in ? -q[j].w : q[j].w);
-            y0 = xstep(y0, 4, w4);
-            y1 = xstep(y1, 4, w4);
-            y0 = xstep(y0, 2, w2);
-            y1 = xstep(y1, 2, w2);
-            y0 = xstep(y0, 1, make_float2(1.f, 0.f));
-            y1 = xstep(y1, 1, make_float2(1.f, 0.f));
-            const float2 t = cmul(y1, w16);
-            const float2 lo = cadd(y0, t), hi = csub(y0, t);
-            if (live) {
-                float2* d = out + row * 16;
+            const int64_t row = r0 + j * RPL + lane / G;
+            float2 y[2] = {make_float2(q[j].x, conj_in ? -q[j].y : q[j].y),
+                           make_float2(q[j].z, conj_in ? -q[j].w : q[j].w)};
+#pragma unroll
+            for (int st = 0; st < LG; ++st) {
+                const int h = G >> (st + 1);
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const float2 p = make_float2(__shfl_xor_sync(0xffffffffu, y[u].x, h, G),
+                                                 __shfl_xor_sync(0xffffffffu, y[u].y, h, G));
+                    y[u] = (i & h) ? (h > 1 ? cmul(csub(p, y[u]), wstep[st]) : csub(p, y[u])) : cadd(y[u], p);
+                }
+            }
+            const float2 t = cmul(y[1], wl);
+            const float2 lo = cadd(y[0], t), hi = csub(y[0], t);
+            if (row < nrows) {
+                float2* d = out + row * L;
                 __stcs(d + k1, make_float2(lo.x * osr, lo.y * osi));
-                __stcs(d + k1 + 8, make_float2(hi.x * osr, hi.y * osi));
+                __stcs(d + k1 + G, make_float2(hi.x * osr, hi.y * osi));
             }
         }
     }
 }
 
-// Rows of 16 points, adjacent in memory (row f at f * 16), 16-byte aligned,
-// without W_N twiddles or bit-reversed addressing: the shuffle kernel.
-static cudaError_t launch_rows16_shfl(const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
+// Adjacent rows of 16..64 points (row f at f * L), 16-byte aligned, without
+// W_N twiddles or bit-reversed addressing: the shuffle kernel.
+static cudaError_t launch_rows_shfl(int log2l, const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
+    if (log2l < 4 || log2l > 6) return cudaErrorNotSupported;
+    const int64_t L = int64_t(1) << log2l;
     const int64_t inner = int64_t(1) << a.inner_log2;
     if (((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) || a.in_stride != 1 ||
         a.out_stride != 1 || a.in_elem_bitrev || a.out_elem_bitrev || a.tw_mode != 0 || a.in_base_bits ||
         a.out_base_bits)
         return cudaErrorNotSupported;
     auto adjacent = [&](int64_t outer, int64_t inner_stride) {
-        return inner == 1 ? outer == 16 : (inner_stride == 16 && outer == inner * 16);
+        return inner == 1 ? outer == L : (inner_stride == L && outer == inner * L);
     };
     if (!adjacent(a.in_outer, a.in_inner) || !adjacent(a.out_outer, a.out_inner)) return cudaErrorNotSupported;
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = device_sm_count(dev, &sms);
     if (e != cudaSuccess) return e;
-    int64_t blocks = ((a.nsub + 31) / 32 + 7) / 8;  // a warp per 32 rows, 8 warps per block
+    const int64_t rows_per_warp = 8 * (64 / L);
+    int64_t blocks = ((a.nsub + rows_per_warp - 1) / rows_per_warp + 7) / 8;  // 8 warps per block
     if (blocks > (int64_t)sms * 8) blocks = (int64_t)sms * 8;
     if (blocks < 1) blocks = 1;
-    k_rows16_shfl<<<(unsigned)blocks, 256, 0, s>>>(in, out, a.nsub, a.conj_in, a.conj_out, a.scale);
+    switch (log2l) {
+        case 4: k_rows_shfl<4><<<(unsigned)blocks, 256, 0, s>>>(in, out, a.nsub, a.conj_in, a.conj_out, a.scale); break;
+        case 5: k_rows_shfl<5><<<(unsigned)blocks, 256, 0, s>>>(in, out, a.nsub, a.conj_in, a.conj_out, a.scale); break;
+        case 6: k_rows_shfl<6><<<(unsigned)blocks, 256, 0, s>>>(in, out, a.nsub, a.conj_in, a.conj_out, a.scale); break;
+        default: return cudaErrorNotSupported;
+    }
     return cudaGetLastError();
 }
 
@@ -1102,7 +1120,7 @@ cudaError_t launch_pass(int log2l, int layout, int lmap, int smap, const float2*
         const cudaError_t e = launch_pass_tma(log2l, in, out, a, s);
         if (e != cudaErrorNotSupported) return e;
     } else if (smap != 2) {  // row tiles with row outputs: bulk-copy pass when the shape allows it
-        cudaError_t e = log2l == 4 ? launch_rows16_shfl(in, out, a, s) : launch_rows_regs(log2l, in, out, a, s);
+        cudaError_t e = log2l == 1 ? launch_rows_regs(log2l, in, out, a, s) : launch_rows_shfl(log2l, in, out, a, s);
         if (e != cudaErrorNotSupported) return e;
         e = launch_pass_tma_rows(log2l, in, out, a, s);
         if (e != cudaErrorNotSupported) return e;
