@@ -1026,11 +1026,17 @@ __global__ void __launch_bounds__(256) k_rows_shfl(const float2* __restrict__ in
     constexpr int L = 1 << LOG2L, G = L / 2, LG = LOG2L - 1, RPL = 32 / G;  // rows per load
     const int lane = threadIdx.x & 31, i = lane & (G - 1);
     const int k1 = LG ? (int)(__brev((unsigned)i) >> (32 - LG)) : 0;
-    float2 wstep[LG > 0 ? LG : 1];  // step q (h = G >> (q + 1)): W_{2h}^(i mod h)
+    // step q (h = G >> (q + 1)), branch-free: y <- (p + sgn y) * w with
+    // sgn = +1, w = 1 on the lower lane of a pair and sgn = -1,
+    // w = W_{2h}^(i mod h) on the upper one
+    float2 wstep[LG > 0 ? LG : 1];
+    float sgn[LG > 0 ? LG : 1];
 #pragma unroll
     for (int q = 0; q < LG; ++q) {
         const int h = G >> (q + 1);
-        wstep[q] = g_tw_levels[2 * h + (i & (h - 1))];
+        const bool upper = i & h;
+        sgn[q] = upper ? -1.f : 1.f;
+        wstep[q] = upper ? g_tw_levels[2 * h + (i & (h - 1))] : make_float2(1.f, 0.f);
     }
     const float2 wl = g_tw_levels[L + k1];  // W_L^k1
     const float osr = scale, osi = conj_out ? -scale : scale;
@@ -1056,7 +1062,8 @@ __global__ void __launch_bounds__(256) k_rows_shfl(const float2* __restrict__ in
                 for (int u = 0; u < 2; ++u) {
                     const float2 p = make_float2(__shfl_xor_sync(0xffffffffu, y[u].x, h, G),
                                                  __shfl_xor_sync(0xffffffffu, y[u].y, h, G));
-                    y[u] = (i & h) ? (h > 1 ? cmul(csub(p, y[u]), wstep[st]) : csub(p, y[u])) : cadd(y[u], p);
+                    const float2 d = make_float2(fmaf(sgn[st], y[u].x, p.x), fmaf(sgn[st], y[u].y, p.y));
+                    y[u] = h > 1 ? cmul(d, wstep[st]) : d;
                 }
             }
             const float2 t = cmul(y[1], wl);
@@ -1070,10 +1077,72 @@ __global__ void __launch_bounds__(256) k_rows_shfl(const float2* __restrict__ in
     }
 }
 
-// Adjacent rows of 16..64 points (row f at f * L), 16-byte aligned, without
+// 128-point rows: the same scheme with four elements per lane.  Lane i of
+// the warp holds x[4i + s] (s < 4, two 16-byte loads), the four 32-point DFTs
+// Ys over i run across all 32 lanes (five shfl_xor steps), and lane i forms
+// X[k1 + 32 k2] = DFT4_s(W128^(s k1) Ys[k1])[k2] for k1 = bitrev5(i).  A warp
+// takes 4 rows per iteration, eight loads in flight.
+__global__ void __launch_bounds__(256) k_rows_shfl128(const float2* __restrict__ in, float2* __restrict__ out,
+                                                      int64_t nrows, int conj_in, int conj_out, float scale) {
+    const int i = threadIdx.x & 31;
+    const int k1 = (int)(__brev((unsigned)i) >> 27);
+    float2 wstep[5];
+    float sgn[5];
+#pragma unroll
+    for (int q = 0; q < 5; ++q) {
+        const int h = 16 >> q;
+        const bool upper = i & h;
+        sgn[q] = upper ? -1.f : 1.f;
+        wstep[q] = upper ? g_tw_levels[2 * h + (i & (h - 1))] : make_float2(1.f, 0.f);
+    }
+    const float2 w1 = g_tw_levels[128 + k1], w2 = g_tw_levels[128 + 2 * k1], w3 = g_tw_levels[128 + 3 * k1];
+    const float osr = scale, osi = conj_out ? -scale : scale;
+    const int64_t groups = (nrows + 3) >> 2;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t g = warp; g < groups; g += nwarps) {
+        const int64_t r0 = g << 2;
+        float4 q[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int64_t row = r0 + (j >> 1);
+            q[j] = row < nrows ? __ldg(reinterpret_cast<const float4*>(in + row * 128) + 2 * i + (j & 1))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int64_t row = r0 + r;
+            const float4 a = q[2 * r], b = q[2 * r + 1];
+            float2 y[4] = {make_float2(a.x, conj_in ? -a.y : a.y), make_float2(a.z, conj_in ? -a.w : a.w),
+                           make_float2(b.x, conj_in ? -b.y : b.y), make_float2(b.z, conj_in ? -b.w : b.w)};
+#pragma unroll
+            for (int st = 0; st < 5; ++st) {
+                const int h = 16 >> st;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float2 p = make_float2(__shfl_xor_sync(0xffffffffu, y[u].x, h),
+                                                 __shfl_xor_sync(0xffffffffu, y[u].y, h));
+                    const float2 d = make_float2(fmaf(sgn[st], y[u].x, p.x), fmaf(sgn[st], y[u].y, p.y));
+                    y[u] = h > 1 ? cmul(d, wstep[st]) : d;
+                }
+            }
+            y[1] = cmul(y[1], w1);
+            y[2] = cmul(y[2], w2);
+            y[3] = cmul(y[3], w3);
+            Dft<4, true>::run(y);
+            if (row < nrows) {
+                float2* d = out + row * 128;
+#pragma unroll
+                for (int k2 = 0; k2 < 4; ++k2) __stcs(d + k1 + 32 * k2, make_float2(y[k2].x * osr, y[k2].y * osi));
+            }
+        }
+    }
+}
+
+// Adjacent rows of 16..128 points (row f at f * L), 16-byte aligned, without
 // W_N twiddles or bit-reversed addressing: the shuffle kernel.
 static cudaError_t launch_rows_shfl(int log2l, const float2* in, float2* out, const PassArgs& a, cudaStream_t s) {
-    if (log2l < 4 || log2l > 6) return cudaErrorNotSupported;
+    if (log2l < 4 || log2l > 7) return cudaErrorNotSupported;
     const int64_t L = int64_t(1) << log2l;
     const int64_t inner = int64_t(1) << a.inner_log2;
     if (((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) || a.in_stride != 1 ||
@@ -1088,7 +1157,7 @@ static cudaError_t launch_rows_shfl(int log2l, const float2* in, float2* out, co
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = device_sm_count(dev, &sms);
     if (e != cudaSuccess) return e;
-    const int64_t rows_per_warp = 8 * (64 / L);
+    const int64_t rows_per_warp = L == 128 ? 4 : 8 * (64 / L);
     int64_t blocks = ((a.nsub + rows_per_warp - 1) / rows_per_warp + 7) / 8;  // 8 warps per block
     if (blocks > (int64_t)sms * 8) blocks = (int64_t)sms * 8;
     if (blocks < 1) blocks = 1;
@@ -1096,6 +1165,7 @@ static cudaError_t launch_rows_shfl(int log2l, const float2* in, float2* out, co
         case 4: k_rows_shfl<4><<<(unsigned)blocks, 256, 0, s>>>(in, out, a.nsub, a.conj_in, a.conj_out, a.scale); break;
         case 5: k_rows_shfl<5><<<(unsigned)blocks, 256, 0, s>>>(in, out, a.nsub, a.conj_in, a.conj_out, a.scale); break;
         case 6: k_rows_shfl<6><<<(unsigned)blocks, 256, 0, s>>>(in, out, a.nsub, a.conj_in, a.conj_out, a.scale); break;
+        case 7: k_rows_shfl128<<<(unsigned)blocks, 256, 0, s>>>(in, out, a.nsub, a.conj_in, a.conj_out, a.scale); break;
         default: return cudaErrorNotSupported;
     }
     return cudaGetLastError();
