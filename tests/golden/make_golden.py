@@ -1,7 +1,7 @@
 """Generate golden vectors by running the Kunlunxin-FFT reference itself.
 
-Run in a container that has the read-only reference tree (default
-``/root/reference``) and Triton; the reference's Triton kernels execute on the
+Run in a container that has the read-only reference tree (``--ref``, or the
+``BFFT_REFERENCE_ROOT`` environment variable) and Triton; the reference's Triton kernels execute on the
 CPU through ``TRITON_INTERPRET=1``.  The output, ``reference_vectors.npz`` plus
 ``reference_plans.json``, is committed next to this script so the GPU box
 (which has no reference tree) and the CPU test suite can use it.
@@ -13,7 +13,7 @@ CPU tensors (its validation requires ``device.type == 'cuda'``).
 
 Usage::
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref PATH_TO_REFERENCE]
 """
 from __future__ import annotations
 
@@ -170,7 +170,7 @@ def _cplx(rng, shape):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("BFFT_REFERENCE_ROOT", "/root/reference"))
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
 
