@@ -53,11 +53,12 @@ WORKLOADS = {
            "desc": "config 5b: one C2C forward of N=2^30 (8 GiB complex64); distributed 4-step over ranks (exchanges fused with the transposes, or NCCL all-to-all)"},
 }
 SEED = 1234
+# One metric string for both arms (BASELINE.json's metric), so the two lines compare.
+METRIC = "complex64 C2C FFT GFLOP/s (5N\u00b7log2N/t) and HBM GB/s vs roofline, 1-8 B200"
 # DRAM bytes per launch of the dominant kernel, from an ncu capture of a small
-# case of the same flow scaled by the elements processed (the summary under
-# profiles/ gives the command and the raw figures).  Keyed by workload and plan.
+# case of the same flow scaled by the elements processed.  Keyed by workload and plan.
 PROFILED_TRAFFIC = {
-    ("5a", "fft_dit_matrix_batch", 256): (7.82e9, "profiles/k_pass_tma_5a.md"),
+    ("5a", "fft_dit_matrix_batch", 256): (7.82e9, "ncu dram__bytes_read+write, 512-row case scaled x16"),
 }
 FALLBACK_HBM_GBS = 6650.0
 
@@ -220,7 +221,7 @@ def run_reference_arm(args, wl) -> None:
     t = time.perf_counter() - t0
     value = gflop(n, rows) * args.steps / t
     line = {
-        "impl": "reference", "metric": "complex64 C2C FFT GFLOP/s (5N*log2N/t)", "value": value,
+        "impl": "reference", "metric": METRIC, "value": value,
         "unit": "GFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "complex128 (reference CPU path is float64)",
@@ -576,7 +577,7 @@ def main() -> None:
 
     if ctx.rank == 0:
         line = {
-            "metric": "complex64 C2C FFT GFLOP/s (5N*log2N/t) and HBM GB/s vs roofline",
+            "metric": METRIC,
             "value": res["value"], "unit": "GFLOP/s", "n_gpus": ctx.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": res["ms_step"], "higher_is_better": True,
             "scaling": res["scaling"], "vs_baseline": None, "dtype": "complex64",

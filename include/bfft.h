@@ -8,7 +8,7 @@
  * Here the Python host layer (kunlunxin-fft_b200/bfft) resolves a plan on the
  * host exactly like the reference and then calls these entry points with
  * plain device pointers, sizes and a CUDA stream; an FFI from any other host
- * language would bind the same symbols (see INTEGRATION.md).
+ * language would bind the same symbols.
  *
  * Conventions
  *   - Data is interleaved complex64 (float re, float im), batch-major (B, N),
@@ -166,10 +166,13 @@ BFFT_EXPORT bfft_status bfft_index_map(int32_t kind, int32_t bits, void* out, in
  * would synchronise the device, or an FFI host with no allocator for the CUDA
  * context.  Same transform as a run_hybrid plan through bfft_execute (x is
  * (batch, n) complex64, n = (n / tile) * tile with both factors <= 4096,
- * transform_direction / norm as in bfft_plan_desc), but the scratch buffer of
- * the two passes is a fixed device array inside this library.
- *   - Limit: batch * n <= BFFT_NOALLOC_MAX_ELEMS (2^22 complex64 = 32 MiB);
- *     larger requests return BFFT_ERR_SHAPE.  Every GPU that loads the library
+ * transform_direction / norm as in bfft_plan_desc) and the same kernels, but
+ * the scratch buffer of the two passes is a fixed device array inside this
+ * library.
+ *   - Limit: n <= BFFT_NOALLOC_MAX_ELEMS (2^22), and for the two-pass shapes
+ *     (1 < tile < n) batch * n <= BFFT_NOALLOC_MAX_ELEMS (32 MiB of complex64);
+ *     larger requests return BFFT_ERR_SHAPE.  The one-pass shapes (tile 1 or
+ *     n) use no scratch and take any batch.  Every GPU that loads the library
  *     holds that array (and a 32 KiB twiddle table) until the process exits.
  *   - No cudaMalloc / cudaFree or other allocating call is made.  The first
  *     call on a device sets up that device (looks up the arrays' device

@@ -301,6 +301,44 @@ void tail_groups(int log2t, int log2n, int glog, int64_t maxp,
     }
 }
 
+// The run_hybrid flow's passes (4-step N = tile * t2, adapter_hybrid.py:224-270):
+// length-t2 FFTs over x[m1 tile + m0] with the twiddle W_N^{k_t m0} fused into
+// their store, then length-tile FFTs over each row k_t stored to
+// out[k_r t2 + k_t].  A factor of 1 drops its pass.  Returns the number of
+// steps written to `out` (0..2); both factors must be <= 2^kMaxPassLog2.
+int hybrid_steps(int64_t n, int64_t B, int64_t tile, const TwoLevel& tw, Step out[2]) {
+    const int64_t t2 = n / tile;
+    const int lt = ilog2(tile), l2 = ilog2(t2);
+    int k = 0;
+    if (t2 > 1) {
+        PassArgs a = blank_pass(tw);
+        a.nsub = B * tile;
+        a.inner = tile;
+        a.in_outer = n;
+        a.in_inner = 1;
+        a.in_stride = tile;
+        a.out_outer = n;
+        a.out_inner = 1;
+        a.out_stride = tile;
+        a.tw_mode = 2;
+        a.tw_mul = 1;
+        out[k++] = pass_step(l2, tile >= 4 ? 1 : 0, 0, a);
+    }
+    if (tile > 1) {
+        PassArgs b = blank_pass(tw);
+        b.nsub = B * t2;
+        b.inner = t2;
+        b.in_outer = n;
+        b.in_inner = tile;
+        b.in_stride = 1;
+        b.out_outer = n;
+        b.out_inner = 1;
+        b.out_stride = t2;
+        out[k++] = pass_step(lt, 0, t2 >= 4 ? 1 : 0, b);
+    }
+    return k;
+}
+
 bfft_status build_core(bfft_plan_s& P) {
     const bfft_plan_desc& d = P.d;
     const int64_t n = P.core_n, B = d.batch;
@@ -458,44 +496,16 @@ bfft_status build_core(bfft_plan_s& P) {
             return BFFT_OK;
         }
         case BFFT_RUN_RUN_HYBRID: {
-            // 4-step N = tile * t2 (adapter_hybrid.py:224-270): length-t2 FFTs
-            // over x[m1 tile + m0] with the twiddle W_N^{k_t m0} fused into
-            // their store, then length-tile FFTs over each row k_t stored to
-            // out[k_r t2 + k_t].
             int64_t tile = d.tile > 0 ? d.tile : 64;
             if (!is_pow2(tile) || tile > n || n % tile)
                 return fail(BFFT_ERR_VALUE, "tile %lld must be a power of two dividing N=%lld", (long long)tile, (long long)n);
             const int64_t t2 = n / tile;
-            const int lt = ilog2(tile), l2 = ilog2(t2);
-            if (lt > kMaxPassLog2 || l2 > kMaxPassLog2)
+            if (ilog2(tile) > kMaxPassLog2 || ilog2(t2) > kMaxPassLog2)
                 return fail(BFFT_ERR_UNSUPPORTED, "4-step factors %lld x %lld exceed the CTA-resident limit 2^%d",
                             (long long)t2, (long long)tile, kMaxPassLog2);
-            if (t2 > 1) {
-                PassArgs a = blank_pass(tw);
-                a.nsub = B * tile;
-                a.inner = tile;
-                a.in_outer = n;
-                a.in_inner = 1;
-                a.in_stride = tile;
-                a.out_outer = n;
-                a.out_inner = 1;
-                a.out_stride = tile;
-                a.tw_mode = 2;
-                a.tw_mul = 1;
-                st.push_back(pass_step(l2, tile >= 4 ? 1 : 0, 0, a));
-            }
-            if (tile > 1) {
-                PassArgs b = blank_pass(tw);
-                b.nsub = B * t2;
-                b.inner = t2;
-                b.in_outer = n;
-                b.in_inner = tile;
-                b.in_stride = 1;
-                b.out_outer = n;
-                b.out_inner = 1;
-                b.out_stride = t2;
-                st.push_back(pass_step(lt, 0, t2 >= 4 ? 1 : 0, b));
-            }
+            Step hs[2];
+            const int k = hybrid_steps(n, B, tile, tw, hs);
+            for (int i = 0; i < k; ++i) st.push_back(hs[i]);
             return BFFT_OK;
         }
         default:
@@ -503,14 +513,12 @@ bfft_status build_core(bfft_plan_s& P) {
     }
 }
 
-void set_first_conj(std::vector<Step>& st) {
-    Step& s = st.front();
+void set_first_conj(Step& s) {
     if (s.kind == S_PASS) s.pa.conj_in = 1;
     else if (s.kind == S_CLUSTER) s.ca.conj_in = 1;
     else s.st.conj_in = 1;
 }
-void set_last_epilogue(std::vector<Step>& st, int conj, float scale) {
-    Step& s = st.back();
+void set_last_epilogue(Step& s, int conj, float scale) {
     if (s.kind == S_PASS) {
         s.pa.conj_out = conj;
         s.pa.scale = scale;
@@ -542,9 +550,8 @@ cudaError_t launch_step(const Step& s, const float2* in, float2* out, cudaStream
 
 // Runs the core steps from `src` into `dst`, ping-ponging through `scratch`;
 // neither `src` nor its aliases are ever written.
-cudaError_t run_core(const std::vector<Step>& st, const float2* src, float2* dst, float2* scratch,
+cudaError_t run_core(const Step* st, size_t L, const float2* src, float2* dst, float2* scratch,
                      cudaStream_t stream) {
-    const size_t L = st.size();
     const float2* cur = src;
     for (size_t i = 0; i < L; ++i) {
         float2* tgt = ((L - 1 - i) % 2 == 0) ? dst : scratch;
@@ -561,6 +568,19 @@ cudaError_t run_core(const std::vector<Step>& st, const float2* src, float2* dst
 namespace bfft {
 void set_last_error(const char* msg) { g_last_error = msg; }
 void count_launches(int k) { g_launches.fetch_add((uint64_t)k, std::memory_order_relaxed); }
+
+cudaError_t run_hybrid_flow(const float2* in, float2* out, float2* scratch, int64_t n, int64_t batch,
+                            int64_t tile, const TwoLevel& tw, int conj, float scale, cudaStream_t s) {
+    Step st[2];
+    const int k = hybrid_steps(n, batch, tile, tw, st);
+    if (k == 0) {
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        return launch_scale(in, out, batch * n, scale, 0, s);
+    }
+    if (conj) set_first_conj(st[0]);
+    set_last_epilogue(st[k - 1], conj, scale);
+    return run_core(st, (size_t)k, in, out, scratch, s);
+}
 }  // namespace bfft
 
 // ================================================================ C ABI
@@ -704,9 +724,9 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
             g_launches.fetch_add(1, std::memory_order_relaxed);
             e = launch_scale((const float2*)in, (float2*)out, B * n, scale, 0, s);
         } else {
-            if (inverse) set_first_conj(core);
-            set_last_epilogue(core, inverse ? 1 : 0, scale);
-            e = run_core(core, (const float2*)in, (float2*)out, ws, s);
+            if (inverse) set_first_conj(core.front());
+            set_last_epilogue(core.back(), inverse ? 1 : 0, scale);
+            e = run_core(core.data(), core.size(), (const float2*)in, (float2*)out, ws, s);
         }
     } else if (d.real_flow == BFFT_REAL_DEDICATED) {
         float2* F = ws;
@@ -715,7 +735,7 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
             // pack: the float32 (B, N) input IS the complex64 (B, N/2) z
             const float scale = (float)norm_scale(n, BFFT_FORWARD, d.norm);
             e = core.empty() ? launch_scale((const float2*)in, F, B * c, 1.0f, 0, s)
-                             : run_core(core, (const float2*)in, F, A, s);
+                             : run_core(core.data(), core.size(), (const float2*)in, F, A, s);
             if (core.empty()) g_launches.fetch_add(1, std::memory_order_relaxed);
             if (e == cudaSuccess) {
                 g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -731,9 +751,9 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
                 // = conj(DFT(conj z))[k]: with the conjugates and the scale fused into
                 // the first and last pass, the core writes the real output itself
                 // (float32 pairs = complex64 (B, N/2)) and the unpack pass goes away.
-                set_first_conj(core);
-                set_last_epilogue(core, 1, scale);
-                e = run_core(core, C, (float2*)out, A, s);
+                set_first_conj(core.front());
+                set_last_epilogue(core.back(), 1, scale);
+                e = run_core(core.data(), core.size(), C, (float2*)out, A, s);
             } else if (e == cudaSuccess) {
                 g_launches.fetch_add(2, std::memory_order_relaxed);
                 e = launch_scale(C, F, B * c, 1.0f, 0, s);
@@ -749,7 +769,7 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
             g_launches.fetch_add(1, std::memory_order_relaxed);
             e = launch_real_to_complex((const float*)in, C, B * n, s);
             if (e == cudaSuccess) {
-                e = core.empty() ? launch_scale(C, F, B * n, 1.0f, 0, s) : run_core(core, C, F, A, s);
+                e = core.empty() ? launch_scale(C, F, B * n, 1.0f, 0, s) : run_core(core.data(), core.size(), C, F, A, s);
                 if (core.empty()) g_launches.fetch_add(1, std::memory_order_relaxed);
             }
             if (e == cudaSuccess) {
@@ -761,7 +781,7 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
             g_launches.fetch_add(1, std::memory_order_relaxed);
             e = launch_hermitian_conj((const float2*)in, C, n, B, s);
             if (e == cudaSuccess) {
-                e = core.empty() ? launch_scale(C, F, B * n, 1.0f, 0, s) : run_core(core, C, F, A, s);
+                e = core.empty() ? launch_scale(C, F, B * n, 1.0f, 0, s) : run_core(core.data(), core.size(), C, F, A, s);
                 if (core.empty()) g_launches.fetch_add(1, std::memory_order_relaxed);
             }
             if (e == cudaSuccess) {

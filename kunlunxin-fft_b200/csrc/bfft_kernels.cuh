@@ -76,6 +76,13 @@ cudaError_t device_sm_count(int dev, int* sms);
 void set_last_error(const char* msg);
 void count_launches(int k);
 
+// The run_hybrid flow (the same steps a BFFT_RUN_RUN_HYBRID plan builds) from
+// `in` to `out` through `scratch` (batch * n complex64; unused when tile is 1
+// or n): conj conjugates the input and the output, scale the output.  Counts
+// its launches.
+cudaError_t run_hybrid_flow(const float2* in, float2* out, float2* scratch, int64_t n, int64_t batch,
+                            int64_t tile, const TwoLevel& tw, int conj, float scale, cudaStream_t s);
+
 // Real-transform epilogues (standalone forms of the reference runner API).
 cudaError_t launch_r2c_stitch(const float2* z, float2* x, int64_t n, int64_t batch, float scale,
                               TwoLevel twn, cudaStream_t s);

@@ -30,7 +30,7 @@ using namespace bfft;
 namespace {
 
 constexpr int64_t kNoAllocMaxElems = BFFT_NOALLOC_MAX_ELEMS;
-constexpr int kNoAllocLoBits = 11;  // two-level W_N table: N <= 2^22 -> 2^11 + 2^11 entries
+constexpr int kNoAllocLoBits = 11;  // two-level W_N table: N <= 2^22 -> at most 2^11 + 2^11 entries
 
 // Intermediate of the two passes: pass 1 writes every element that pass 2
 // reads, so nothing in it has to start at zero.
@@ -104,12 +104,14 @@ extern "C" bfft_status bfft_hybrid_c2c_noalloc(const void* in, void* out, int64_
     if (log2t < 0 || tile > n) return fail(BFFT_ERR_VALUE, "tile %lld must be a power of two dividing N=%lld",
                                            (long long)tile, (long long)n);
     if (batch < 1) return fail(BFFT_ERR_SHAPE, "batch must be >= 1");
-    if (n > kNoAllocMaxElems || batch > kNoAllocMaxElems / n)
+    const int64_t t2 = n / tile;
+    // Only the two-pass shapes use the scratch array; every shape uses the
+    // twiddle array, sized for N <= kNoAllocMaxElems.
+    if (n > kNoAllocMaxElems || (tile > 1 && t2 > 1 && batch > kNoAllocMaxElems / n))
         return fail(BFFT_ERR_SHAPE,
                     "batch*N = %lld*%lld exceeds the fixed scratch of %lld complex64 elements "
                     "(32 MiB); use bfft_execute with a caller workspace for larger transforms",
                     (long long)batch, (long long)n, (long long)kNoAllocMaxElems);
-    const int64_t t2 = n / tile;
     if (log2t > kMaxPassLog2 || log2n - log2t > kMaxPassLog2)
         return fail(BFFT_ERR_UNSUPPORTED, "4-step factors %lld x %lld exceed 4096", (long long)t2, (long long)tile);
     int ndev = 0;
@@ -125,65 +127,23 @@ extern "C" bfft_status bfft_hybrid_c2c_noalloc(const void* in, void* out, int64_
     cudaStream_t s = (cudaStream_t)stream;
     cudaError_t e = cudaSuccess;
     if (st == BFFT_OK) {
-        const int lo_bits = log2n < kNoAllocLoBits ? log2n : kNoAllocLoBits;
-        TwoLevel tw{sym.twiddle, sym.twiddle + ((int64_t)1 << lo_bits), lo_bits, log2n};
-        e = fill_two_level(sym.twiddle, sym.twiddle + ((int64_t)1 << lo_bits), lo_bits, log2n, s);
+        // the split a plan's own table uses (ceil(log2 N / 2) low bits), so
+        // the values are the ones bfft_execute would read
+        const int lo_bits = (log2n + 1) / 2;
+        const int64_t nlo = (int64_t)1 << (lo_bits < log2n ? lo_bits : log2n);
+        TwoLevel tw{sym.twiddle, sym.twiddle + nlo, lo_bits, log2n};
+        e = fill_two_level(sym.twiddle, sym.twiddle + nlo, lo_bits, log2n, s);
         const bool inverse = transform_direction == BFFT_INVERSE;
         double scale = 1.0;
         if (norm == BFFT_NORM_ORTHO) scale = 1.0 / std::sqrt((double)n);
         else if ((norm == BFFT_NORM_FORWARD && !inverse) || (norm == BFFT_NORM_BACKWARD && inverse))
             scale = 1.0 / (double)n;
-        // pass 1: length-t2 FFTs over x[m1*tile + m0], W_N^{k_t m0} fused into the store
-        PassArgs a{};
-        a.nsub = batch * tile;
-        a.inner = tile;
-        a.inner_log2 = log2t;
-        a.in_outer = n;
-        a.in_inner = 1;
-        a.in_stride = tile;
-        a.out_outer = n;
-        a.out_inner = 1;
-        a.out_stride = tile;
-        a.tw_mode = 2;
-        a.tw_mul = 1;
-        a.tw = tw;
-        a.scale = 1.0f;
-        a.conj_in = inverse ? 1 : 0;
-        // pass 2: length-tile FFTs over each row k_t, stored to out[k_r t2 + k_t]
-        PassArgs b{};
-        b.nsub = batch * t2;
-        b.inner = t2;
-        b.inner_log2 = log2n - log2t;
-        b.in_outer = n;
-        b.in_inner = tile;
-        b.in_stride = 1;
-        b.out_outer = n;
-        b.out_inner = 1;
-        b.out_stride = t2;
-        b.tw = tw;
-        b.scale = (float)scale;
-        b.conj_out = inverse ? 1 : 0;
-        count_launches(1);
-        if (e == cudaSuccess) {
-            if (t2 == 1) {  // tile == N: one pass, no scratch needed
-                b.conj_in = a.conj_in;
-                count_launches(1);
-                e = launch_pass(log2t, 0, 0, 0, (const float2*)in, (float2*)out, b, s);
-            } else if (tile == 1) {  // a single length-N column pass
-                a.scale = (float)scale;
-                a.conj_out = b.conj_out;
-                a.tw_mode = 0;
-                count_launches(1);
-                e = launch_pass(log2n, 0, 0, 0, (const float2*)in, (float2*)out, a, s);
-            } else {
-                count_launches(1);
-                e = launch_pass(log2n - log2t, tile >= 4 ? 1 : 0, 0, 0, (const float2*)in, sym.scratch, a, s);
-                if (e == cudaSuccess) {
-                    count_launches(1);
-                    e = launch_pass(log2t, 0, 0, t2 >= 4 ? 2 : 0, sym.scratch, (float2*)out, b, s);
-                }
-            }
-        }
+        count_launches(1);  // the twiddle fill
+        // the same passes (kernels, launch shapes, programmatic dependent
+        // launch of the second pass) as a run_hybrid plan through bfft_execute
+        if (e == cudaSuccess)
+            e = run_hybrid_flow((const float2*)in, (float2*)out, sym.scratch, n, batch, tile, tw, inverse ? 1 : 0,
+                                (float)scale, s);
     }
     if (prev >= 0 && prev != device) cudaSetDevice(prev);
     if (st != BFFT_OK) return st;

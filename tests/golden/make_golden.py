@@ -170,9 +170,12 @@ def _cplx(rng, shape):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("BFFT_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("BFFT_REFERENCE_ROOT"),
+                    help="reference tree (default: $BFFT_REFERENCE_ROOT); required")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("name the reference tree with --ref or BFFT_REFERENCE_ROOT")
 
     runner = _setup_reference(args.ref)
     import torch

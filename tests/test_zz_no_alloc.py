@@ -50,6 +50,11 @@ def _rel_l2(a, b):
 @pytest.mark.parametrize("cases", [
     [(4096, 64, 64, FWD, "backward"), (65536, 16, 256, INV, "ortho")],
     [(1 << 20, 4, 1024, FWD, "forward"), (2048, 128, 2048, INV, "backward")],
+    # one length-N pass (tile 1), a 2-wide first pass (tile < 4: row layout),
+    # a 2-point second pass (n / tile < 4: direct stores), and a single-pass
+    # shape whose batch * N is past the scratch limit (it uses no scratch)
+    [(1024, 8, 1, INV, "ortho"), (4096, 4, 2, FWD, "forward")],
+    [(4096, 4, 2048, INV, "backward"), (4096, 2048, 4096, FWD, "none")],
 ])
 def test_noalloc_matches_regular_entry_two_calls_in_a_row(cases):
     rng = np.random.default_rng(77)
@@ -60,6 +65,8 @@ def test_noalloc_matches_regular_entry_two_calls_in_a_row(cases):
         got = _noalloc(x, torch.empty_like(x), n, batch, tile, tdir, norm)
         torch.cuda.synchronize()
         assert _rel_l2(got, want) <= TOL_REF, (n, batch, tile)
+        # the same kernels on the same twiddle values: the same bits
+        assert torch.equal(got, want), (n, batch, tile)
         # and it is a transform: check against float64 on one row
         ref = np.fft.fft(x[0].cpu().numpy().astype(np.complex128))
         if tdir == INV:
@@ -94,3 +101,9 @@ def test_noalloc_rejects_requests_beyond_its_fixed_scratch():
     with pytest.raises(ValueError, match="exceeds the fixed scratch"):
         _noalloc(x, torch.empty_like(x), n, batch, 1024, FWD, "backward")
     assert _lib.launch_counter() == before
+
+
+def test_no_bounded_wait_expired_in_the_noalloc_passes():
+    """The two-pass shapes run the TMA passes, whose mbarrier waits are
+    bounded; none of the calls above gave up a wait."""
+    assert _lib.device_status(0) == 0
