@@ -302,6 +302,16 @@ class Ctx:
             self.dist.all_reduce(t)
         self.torch.cuda.synchronize(self.dev)
 
+    def gather(self, vals: list[float]) -> list[list[float]]:
+        """Every rank's `vals` (same length on all ranks), rank order."""
+        torch = self.torch
+        t = torch.tensor(vals, dtype=torch.float64, device=self.dev)
+        if self.world == 1:
+            return [t.tolist()]
+        out = torch.empty(self.world * len(vals), dtype=torch.float64, device=self.dev)
+        self.dist.all_gather_into_tensor(out, t)
+        return out.view(self.world, len(vals)).tolist()
+
     def max_over_ranks(self, v: float) -> float:
         if self.world == 1:
             return v
@@ -374,6 +384,75 @@ def _e2e(ctx, fn_dev, xh, yh, xd, steps):
     return ctx.max_over_ranks(s2.elapsed_time(e2)) / steps
 
 
+def _numa_node_of_gpu(ctx) -> int | None:
+    """NUMA node the GPU hangs off (sysfs), None when not reported."""
+    try:
+        pr = ctx.torch.cuda.get_device_properties(ctx.dev)
+        bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
+            return int(f.read().strip())
+    except (AttributeError, OSError, ValueError):
+        return None
+
+
+def _host_numa_nodes() -> int | None:
+    """Online NUMA nodes of the host ("0-1" -> 2)."""
+    try:
+        with open("/sys/devices/system/node/online") as f:
+            txt = f.read().strip()
+        count = 0
+        for part in txt.split(","):
+            lo, _, hi = part.partition("-")
+            count += int(hi or lo) - int(lo) + 1
+        return count
+    except (OSError, ValueError):
+        return None
+
+
+def link_rates(ctx, xh, yh) -> dict:
+    """Host<->device copy rates of this step's pinned buffers, each direction
+    alone (CUDA events, two copies each after one untimed), per rank, with
+    where the GPUs and the host memory sit."""
+    torch = ctx.torch
+    xd = torch.empty(tuple(xh.shape), dtype=xh.dtype, device=ctx.dev)
+    yd = torch.empty(tuple(yh.shape), dtype=yh.dtype, device=ctx.dev)
+    rates = []
+    for fn, nbytes in ((lambda: xd.copy_(xh, non_blocking=True), xh.numel() * xh.element_size()),
+                       (lambda: yh.copy_(yd, non_blocking=True), yh.numel() * yh.element_size())):
+        fn()
+        ctx.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(ctx.stream)
+        fn()
+        fn()
+        b.record(ctx.stream)
+        b.synchronize()
+        rates.append(nbytes / (a.elapsed_time(b) / 2 / 1e3) / 1e9)
+        ctx.barrier()
+    del xd, yd
+    node = _numa_node_of_gpu(ctx)
+    per = ctx.gather([rates[0], rates[1], -1.0 if node is None else float(node)])
+    return {"h2d_gbs_per_rank": [round(r[0], 1) for r in per], "d2h_gbs_per_rank": [round(r[1], 1) for r in per],
+            "gpu_numa_node_per_rank": [int(r[2]) if r[2] >= 0 else None for r in per],
+            "host_numa_nodes": _host_numa_nodes(),
+            "pinned_host_buffers": "torch pin_memory=True, first touched by each rank's process (no NUMA binding)",
+            "how": "each direction alone: 2 full-buffer cudaMemcpyAsync per direction on the rank's stream, "
+                   "CUDA events, all ranks at once"}
+
+
+def api_wall(fn, trials: int) -> dict:
+    """The reference's timing protocol (src/xpu/runner.py:1576-1635): warm-up,
+    then interleaved trials of synchronised API wall time, with CUDA-event
+    device time recorded beside it; median / p10 / p90."""
+    from bfft import runner
+
+    r = runner.time_call_detailed(fn, warmup=3, trials=trials, seed=0)
+    return {"api_ms": r["api_ms"], "kernel_ms": r["kernel_ms"],
+            "protocol": "bfft.runner.time_call_detailed: 3 warm-up calls, interleaved trials, "
+                        "torch.cuda.synchronize() after each call; api_ms = host wall time of call + sync"}
+
+
 def run_batch(args, wl, ctx) -> dict:
     """Configs 5a / 3: a batched C2C forward job, rows sharded over ranks."""
     import bfft
@@ -424,6 +503,9 @@ def run_batch(args, wl, ctx) -> dict:
                 "algorithmic_bytes_per_launch": bytes_per_launch,
                 "transform_hbm_gbs": (in_row + out_row) * b / (ms_step / 1e3) / 1e9}
 
+    # the reference's protocol: synchronised API wall time per call
+    wall = api_wall(lambda: bfft.execute_fft_plan(plan, x), trials=args.api_trials)
+
     # end to end: host (pinned) in, host out, through the public host-buffer
     # entry; every step copies its input in and its result out
     from bfft.host_io import default_chunks, execute_fft_plan_host
@@ -451,9 +533,10 @@ def run_batch(args, wl, ctx) -> dict:
            "d2h_bytes_per_step": int(yh.numel() * yh.element_size()) * ctx.world,
            "chunks": chunks,
            "path": "execute_fft_plan_host (bfft public API -> libbfft bfft_stream_execute): pinned host in/out, "
-                   "batch in chunks, copy in / transform / copy out overlapped on three streams"}
+                   "batch in chunks, copy in / transform / copy out overlapped on three streams",
+           "host_links": link_rates(ctx, xh, yh)}
     return {"value": value, "ms_step": ms_step, "launches": launches, "clocks": clocks, "roofline": roofline,
-            "e2e": e2e, "scaling": "strong",
+            "e2e": e2e, "scaling": "strong", "api_wall": wall,
             "config": {"workload": wl["desc"], "n": n, "global_batch": btot, "per_rank_batch": b,
                        "transform": f"{tt}/{td}", "flop_convention": "5 N log2 N" if tt == "c2c" else "2.5 N log2 N",
                        "parallelism": f"batch-shard x{ctx.world} (no data-path collective)",
@@ -534,6 +617,80 @@ def run_4step(args, wl, ctx) -> dict:
             "gflop_per_step": gflop(n, 1)}
 
 
+def secondary_5b(args, ctx) -> dict:
+    """Config 5b beside the 5a headline, so every scaling run records it: one
+    C2C forward of N = 2^30 (the single-GPU four-pass plan on one GPU, the
+    slab-distributed 4-step of bfft.dist.DistributedFFT over the ranks
+    otherwise), timed like the headline (max over ranks of CUDA-event time),
+    and the same path checked at N = 2^24 against float64 numpy.fft on
+    rank 0 (the slabs gathered there)."""
+    import numpy as np
+
+    import bfft
+    from bfft import dist as bdist
+
+    torch = ctx.torch
+    res = {"workload": "config 5b: one C2C forward of N=2^30 (8 GiB complex64), slab per rank",
+           "exchange": None}
+
+    def make(n):
+        if ctx.world == 1:
+            plan, _ = choose_plan(n, 1)
+            return (lambda t: bfft.execute_fft_plan(plan, t)), None, f"{plan.executed} tile {plan.params['tile']}"
+        f = bdist.DistributedFFT(n, device=ctx.dev, exchange=args.exchange)
+        res["exchange"] = f.exchange
+        return f.execute, f, f"DistributedFFT {f.n1}x{f.n2}, {f.exchange} exchanges"
+
+    # parity at N = 2^24
+    nc = 1 << 24
+    g = torch.Generator(device=ctx.dev).manual_seed(SEED + 77 + ctx.rank)
+    xc = torch.complex(torch.randn(nc // ctx.world, device=ctx.dev, generator=g),
+                       torch.randn(nc // ctx.world, device=ctx.dev, generator=g))
+    fn, obj, _ = make(nc)
+    yc = fn(xc)
+    parts = []
+    for t in (xc, yc):
+        flat = torch.view_as_real(t).reshape(-1).contiguous()
+        if ctx.world > 1:
+            full = torch.empty(flat.numel() * ctx.world, dtype=flat.dtype, device=ctx.dev)
+            ctx.dist.all_gather_into_tensor(full, flat)
+        else:
+            full = flat
+        parts.append(full)
+    rel = None
+    if ctx.rank == 0:
+        xa = parts[0].view(-1, 2).cpu().numpy().astype(np.float64)
+        ya = parts[1].view(-1, 2).cpu().numpy().astype(np.float64)
+        ref = np.fft.fft(xa[:, 0] + 1j * xa[:, 1])
+        got = ya[:, 0] + 1j * ya[:, 1]
+        rel = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+    del xc, yc, parts, fn, obj
+    ctx.barrier()
+
+    n = 1 << 30
+    slab = n // ctx.world
+    g = torch.Generator(device=ctx.dev).manual_seed(SEED + ctx.rank)
+    x = torch.complex(torch.randn(slab, device=ctx.dev, generator=g), torch.randn(slab, device=ctx.dev, generator=g))
+    fn, obj, path = make(n)
+    for _ in range(3):
+        y = fn(x)
+    del y
+    ms, launches, clocks = ctx.timed(lambda: fn(x), args.steps_5b)
+    ms /= args.steps_5b
+    res.update({"path": path, "n": n, "ms_per_step": ms, "steps": args.steps_5b, "warmup": 3,
+                "gflops": gflop(n, 1) / (ms / 1e3), "gpu_launches": int(launches),
+                "transform_hbm_gbs_per_gpu": 16.0 * slab / (ms / 1e3) / 1e9,
+                "parity_n": nc, "rel_l2_vs_float64": rel, "clocks": clocks})
+    if ctx.world > 1:
+        wire = 3.0 * 8.0 * slab * (ctx.world - 1) / ctx.world
+        res["nvlink"] = {"bytes_per_step_per_gpu": wire, "gbs_per_direction": wire / (ms / 1e3) / 1e9,
+                         "peak_gbs_per_direction": 770.0, "peak_source": "measured peer copy on this pool"}
+    del x, fn, obj
+    torch.cuda.synchronize(ctx.dev)
+    ctx.barrier()
+    return res
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -542,6 +699,10 @@ def main() -> None:
     ap.add_argument("--impl", choices=("bfft", "reference"), default="bfft")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="5a")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--api-trials", type=int, default=20,
+                    help="trials of the reference-style synchronised API wall-time protocol")
+    ap.add_argument("--steps-5b", type=int, default=5, help="timed steps of the config-5b secondary line")
+    ap.add_argument("--no-5b", action="store_true", help="skip the config-5b secondary measurement (5a only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", choices=("p2p", "nccl"), default=None,
                     help="5b on 2+ GPUs: fused peer-store exchanges (default) or NCCL all-to-alls")
@@ -568,6 +729,9 @@ def main() -> None:
 
     ctx = Ctx(args)
     res = run_4step(args, wl, ctx) if wl.get("kind") == "4step" else run_batch(args, wl, ctx)
+    sec = None
+    if args.workload == "5a" and args.batch is None and not args.no_5b:
+        sec = secondary_5b(args, ctx)
 
     cpu = None
     if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline:
@@ -585,6 +749,10 @@ def main() -> None:
             "config": res["config"], "roofline": res["roofline"], "cpu_baseline": cpu, "e2e": res["e2e"],
             "gpu_launches": int(res["launches"]), "clocks": res["clocks"],
         }
+        if res.get("api_wall") is not None:
+            line["api_wall"] = res["api_wall"]
+        if sec is not None:
+            line["secondary_5b"] = sec
         if wl.get("profile_case"):
             line["profile_case"] = True
         print(json.dumps(line), flush=True)

@@ -1,11 +1,24 @@
-"""Lowering contract for selector-table entries (host-only, no torch).
+"""What the B200 library can lower: the contract selector-table entries must meet.
 
-The reference checks every table entry against the lowering its P800 Triton
-backend accepts (src/xpu/candidates.py:189-383) before the table may be used.
-This module applies the same contract to the B200 lowerings: the same schema-v2
-attribution axes (flow_id / flow_realization / processing_unit /
-local_residence), the same knob rules, with the B200 internal layout
-(interleaved complex64) in place of the P800 planar split.
+A selector-table entry names a point of the design space (schema v2 axes:
+flow_id, flow_realization, processing_unit, local residence, knobs).  The
+reference refuses a table whose entries its own backend cannot lower
+(src/xpu/candidates.py:189-386).  Here the question is what the plan
+builder of this library accepts (``build_core`` in csrc/bfft_api.cu):
+
+* ``global-stage``      -> the one-stage-per-launch cascades: radix-2
+  (``k_radix2_stage``, M0 / M4, spread or folded batch) and radix-4
+  (``k_radix4_stage``, M5, spread batch);
+* ``fused-inplace``     -> a CTA-resident local group of ``fused_tile``
+  points followed by radix-2 stages (M1, single transform);
+* ``matrix-resident``   -> a CTA-resident local group plus tail passes
+  (M2; the batched form is the batch local-fused core, spread batch);
+* ``grouped-boundary``  -> a local group plus the grouped tail (M3, needs
+  ``glog >= 1``).
+
+The accepted combinations are data (``LOWERINGS``); ``check_lowering`` runs
+an ordered list of rules over a candidate and collects one reason per broken
+rule.  An entry is legal when no rule objects.
 """
 from __future__ import annotations
 
@@ -16,33 +29,42 @@ from .semantic import SPECIALIZED_FLOWS
 
 SPECIALIZED_ROUTING = frozenset().union(*SPECIALIZED_FLOWS.values())
 
-_LOCAL_FLOWS = frozenset({"local-fused-tile"})
-_GLOBAL_CORE_FLOWS = frozenset({"baseline-global-stage", "batch-spread", "batch-folded"})
-_BATCH_SPREAD_FLOWS = frozenset({"batch-spread"})
-
+LAYOUT = "interleaved-c64"  # complex64 (re, im) pairs, batch-major -- the only data layout here
 PROCESSING_UNITS = ("radix2-scalar", "radix4-scalar", "dense-dot-fft64", "composite-linear-map")
 UNIT_RADIX = {"radix2-scalar": 2, "radix4-scalar": 4, "dense-dot-fft64": 2, "composite-linear-map": 2}
 FLOW_REALIZATIONS = ("global-stage", "fused-inplace", "matrix-resident", "grouped-boundary")
-REALIZATION_UNITS = {
-    "global-stage": ("radix2-scalar", "radix4-scalar"),
-    "fused-inplace": ("radix2-scalar", "radix4-scalar"),
-    "matrix-resident": ("dense-dot-fft64",),
-    "grouped-boundary": ("composite-linear-map",),
-}
 LOCAL_RESIDENCES = ("none", "cache", "register", "implicit-dot", "register+implicit-dot")
-REALIZATION_LOCAL_RESIDENCES = {
-    "global-stage": ("none",),
-    "fused-inplace": ("none", "cache"),
-    "matrix-resident": ("register", "implicit-dot", "register+implicit-dot"),
-    "grouped-boundary": ("register",),
+
+_STAGE_FLOWS = frozenset({"baseline-global-stage", "batch-spread", "batch-folded"})
+_TILE_FLOWS = frozenset({"local-fused-tile"})
+
+
+@dataclass(frozen=True)
+class Lowering:
+    """One realization as the plan builder implements it."""
+
+    builder: str                 # what runs (for messages)
+    units: tuple                 # processing units it is written for
+    flows: frozenset             # flow ids that route to it (dedicated real flows route everywhere)
+    residences: tuple            # local residences it evidences; the first is the derived default
+    batch_variants: tuple        # 'none' = single transform
+    folded_units: tuple = ()     # units whose folded batch form exists
+    takes_tile: bool = False     # consumes fused_tile > 1
+    needs_glog: bool = False
+
+
+LOWERINGS = {
+    "global-stage": Lowering("one radix-2 / radix-4 stage per launch", ("radix2-scalar", "radix4-scalar"),
+                             _STAGE_FLOWS, ("none",), ("none", "spread", "folded"),
+                             folded_units=("radix2-scalar",)),
+    "fused-inplace": Lowering("CTA-resident local group + radix-2 stages", ("radix2-scalar", "radix4-scalar"),
+                              _TILE_FLOWS, ("cache", "none"), ("none",), takes_tile=True),
+    "matrix-resident": Lowering("CTA-resident local group + tail passes", ("dense-dot-fft64",), _TILE_FLOWS,
+                                ("register+implicit-dot", "register", "implicit-dot"), ("none", "spread"),
+                                takes_tile=True),
+    "grouped-boundary": Lowering("local group + grouped tail passes", ("composite-linear-map",), _TILE_FLOWS,
+                                 ("register",), ("none",), takes_tile=True, needs_glog=True),
 }
-_DERIVED_LOCAL_RESIDENCE = {
-    "global-stage": "none",
-    "fused-inplace": "cache",
-    "matrix-resident": "register+implicit-dot",
-    "grouped-boundary": "register",
-}
-LAYOUT = "interleaved-c64"
 
 
 class LoweringStatus:
@@ -51,17 +73,9 @@ class LoweringStatus:
     INFEASIBLE = "infeasible"
 
 
-def _is_local(flow) -> bool:
-    return flow in _LOCAL_FLOWS or flow in SPECIALIZED_ROUTING
-
-
-def _is_global(flow) -> bool:
-    return flow in _GLOBAL_CORE_FLOWS or flow in SPECIALIZED_ROUTING
-
-
 @dataclass(frozen=True)
 class Candidate:
-    """One point of the design space (schema v2)."""
+    """One point of the design space (schema-v2 fields)."""
 
     flow_id: str
     processing_unit: str
@@ -94,19 +108,19 @@ class Candidate:
 
 
 def effective_flow_realization(c: Candidate) -> str:
+    """The declared realization, else the one the knobs imply."""
     if c.flow_realization:
         return c.flow_realization
-    if c.flow_id in _GLOBAL_CORE_FLOWS:
+    if c.flow_id in _STAGE_FLOWS:
         return "global-stage"
-    if c.glog >= 1:
-        return "grouped-boundary"
-    if c.rows > 1:
-        return "matrix-resident"
-    return "fused-inplace"
+    return "grouped-boundary" if c.glog >= 1 else ("matrix-resident" if c.rows > 1 else "fused-inplace")
 
 
 def effective_local_residence(c: Candidate) -> str:
-    return c.local_residence or _DERIVED_LOCAL_RESIDENCE[effective_flow_realization(c)]
+    if c.local_residence:
+        return c.local_residence
+    low = LOWERINGS.get(effective_flow_realization(c))
+    return low.residences[0] if low else "none"
 
 
 @dataclass(frozen=True)
@@ -120,111 +134,123 @@ class Verdict:
         return self.status == LoweringStatus.LEGAL
 
     def to_dict(self) -> dict:
-        return {"candidate": self.candidate.to_dict(), "status": self.status,
-                "reasons": list(self.reasons)}
+        return {"candidate": self.candidate.to_dict(), "status": self.status, "reasons": list(self.reasons)}
 
 
-def _pow2(name: str, val: int, reasons: list, minimum: int = 1) -> None:
-    if val < minimum or (val & (val - 1)) != 0:
-        reasons.append(f"{name}: must be a power of two >= {minimum}, got {val}")
+# ---------------------------------------------------------------- rules
+#
+# Each rule sees the candidate and its resolved lowering (None when the
+# realization is unknown) and returns the reasons it objects with.
+
+def _pow2(v) -> bool:
+    return isinstance(v, int) and v >= 1 and v & (v - 1) == 0
+
+
+def _routes(flow: str, allowed: frozenset) -> bool:
+    return flow in allowed or flow in SPECIALIZED_ROUTING
+
+
+def _rule_unit(c, low):
+    if c.processing_unit not in UNIT_RADIX:
+        return [f"processing-unit {c.processing_unit!r} has no B200 kernel (kernels exist for "
+                f"{', '.join(PROCESSING_UNITS)})"]
+    if c.radix != UNIT_RADIX[c.processing_unit]:
+        return [f"processing-unit {c.processing_unit!r} runs radix {UNIT_RADIX[c.processing_unit]}, "
+                f"the entry says radix {c.radix}"]
+    return []
+
+
+def _rule_layout(c, low):
+    out = []
+    if c.layout != LAYOUT:
+        out.append(f"layout {c.layout!r}: the kernels read and write {LAYOUT!r} only")
+    if c.boundary_residence != "gm":
+        out.append(f"boundary_residence {c.boundary_residence!r}: passes hand over through device memory ('gm')")
+    return out
+
+
+def _rule_knobs(c, low):
+    out = [f"{name} must be a power of two >= 1, got {val}"
+           for name, val in (("block", c.block), ("fused_tile", c.fused_tile), ("rows", c.rows),
+                             ("cells", c.cells)) if not _pow2(val)]
+    if c.maxp != 0 and not _pow2(c.maxp):
+        out.append(f"maxp must be 0 or a power of two, got {c.maxp}")
+    if c.glog < 0:
+        out.append(f"glog must be >= 0, got {c.glog}")
+    return out
+
+
+def _rule_realization(c, low):
+    real = effective_flow_realization(c)
+    if low is None:
+        return [f"flow_realization {real!r} is not one of {', '.join(FLOW_REALIZATIONS)}"]
+    out = []
+    if not _routes(c.flow_id, low.flows):
+        out.append(f"flow_realization {real!r} ({low.builder}) is reached from "
+                   f"{' / '.join(sorted(low.flows))}, not from flow {c.flow_id!r}")
+    if c.processing_unit in UNIT_RADIX and c.processing_unit not in low.units:
+        out.append(f"processing-unit {c.processing_unit!r} is not what {real!r} runs ({', '.join(low.units)})")
+    res = effective_local_residence(c)
+    if res not in low.residences:
+        out.append(f"local_residence {res!r} is not evidenced by {real!r} ({', '.join(low.residences)})")
+    if low.needs_glog and c.glog < 1:
+        out.append(f"glog {c.glog}: {real!r} groups at least one tail stage (glog >= 1)")
+    return out
+
+
+def _rule_tile(c, low):
+    if c.fused_tile > 1 and not _routes(c.flow_id, _TILE_FLOWS):
+        return [f"fused_tile {c.fused_tile} is a local-group size; flow {c.flow_id!r} has no local group"]
+    if c.fused_tile == 1 and not _routes(c.flow_id, _STAGE_FLOWS):
+        return [f"flow {c.flow_id!r} needs a local group (fused_tile > 1); fused_tile=1 runs only the stage flows"]
+    return []
+
+
+def _rule_batch(c, low):
+    v = c.batch_variant
+    if v == "none":
+        out = []
+        if c.batch != 1:
+            out.append(f"batch {c.batch} needs a batch variant (spread or folded), the entry has none")
+        if c.flow_id in ("batch-spread", "batch-folded"):
+            out.append(f"flow {c.flow_id!r} is a batched flow but batch_variant is 'none'")
+        if (c.ud, c.td) != (1, 1):
+            out.append(f"Ud={c.ud}, Td={c.td}: data expansion exists only with a batch variant")
+        return out
+    if v not in ("spread", "folded"):
+        return [f"batch_variant {v!r}: the batched launches are 'spread' (2-D grid) or 'folded' (flat grid)"]
+    out = [] if _pow2(c.batch) else [f"batch must be a power of two, got {c.batch}"]
+    real = effective_flow_realization(c)
+    if low is not None and v not in low.batch_variants:
+        out.append(f"batch_variant {v!r} has no {real!r} launch ({low.builder})")
+    if v == "spread":
+        if real != "matrix-resident" and not _routes(c.flow_id, frozenset({"batch-spread"})):
+            out.append(f"flow {c.flow_id!r}: the spread stage cascade is flow 'batch-spread'")
+        if (c.ud, c.td) != (c.batch, 1):
+            out.append(f"spread launches one grid row per transform: Ud={c.batch}, Td=1 expected, "
+                       f"got Ud={c.ud}, Td={c.td}")
+    else:
+        if low is not None and c.processing_unit not in low.folded_units:
+            out.append(f"batch_variant 'folded' exists for the radix-2 stage cascade only, not "
+                       f"{real}/{c.processing_unit}")
+        elif c.flow_id != "batch-folded":
+            out.append(f"flow {c.flow_id!r}: the folded stage cascade is flow 'batch-folded'")
+        if (c.ud, c.td) != (1, c.batch):
+            out.append(f"folded launches one flat grid: Ud=1, Td={c.batch} expected, got Ud={c.ud}, Td={c.td}")
+    if c.fused_tile > 1 and not (real == "matrix-resident" and v == "spread"):
+        out.append(f"fused_tile {c.fused_tile}: batched local groups exist only as the matrix-resident spread core")
+    return out
+
+
+def _rule_pipeline(c, low):
+    return [] if c.pipeline == "none" else [f"pipeline {c.pipeline!r}: no such overlap schedule is built"]
+
+
+RULES = (_rule_unit, _rule_layout, _rule_knobs, _rule_realization, _rule_tile, _rule_batch, _rule_pipeline)
 
 
 def check_lowering(c: Candidate, profile: DeviceProfile | None = None) -> Verdict:
-    """Apply the B200 lowering contract; rejections carry their reasons."""
-    reasons: list[str] = []
-    real = effective_flow_realization(c)
-    local_res = effective_local_residence(c)
-
-    if c.processing_unit not in UNIT_RADIX:
-        reasons.append(f"processing-unit: only {', '.join(PROCESSING_UNITS)} are implemented; "
-                       f"{c.processing_unit!r} is not-lowered")
-    elif c.radix not in (2, 4):
-        reasons.append(f"radix: must be 2 or 4, got {c.radix}")
-    elif c.radix != UNIT_RADIX[c.processing_unit]:
-        reasons.append(f"processing-unit: {c.processing_unit!r} must match "
-                       f"radix={UNIT_RADIX[c.processing_unit]} (got radix={c.radix})")
-
-    if c.layout != LAYOUT:
-        reasons.append(f"layout: the B200 lowering accepts {LAYOUT!r}, got {c.layout!r}")
-    if c.boundary_residence != "gm":
-        reasons.append("boundary_residence: passes exchange through device memory ('gm'); "
-                       f"got {c.boundary_residence!r}")
-
-    _pow2("block", c.block, reasons)
-    _pow2("fused_tile", c.fused_tile, reasons)
-    _pow2("rows", c.rows, reasons)
-    _pow2("cells", c.cells, reasons)
-    if c.maxp != 0:
-        _pow2("maxp", c.maxp, reasons)
-    if c.glog < 0:
-        reasons.append(f"glog: must be >= 0, got {c.glog}")
-
-    if real not in FLOW_REALIZATIONS:
-        reasons.append(f"flow_realization: must be one of {', '.join(FLOW_REALIZATIONS)}, got {real!r}")
-    else:
-        local = real != "global-stage"
-        if local and not _is_local(c.flow_id):
-            reasons.append(f"flow_realization: {real!r} requires flow 'local-fused-tile', got {c.flow_id!r}")
-        if not local and not _is_global(c.flow_id):
-            reasons.append(f"flow_realization: 'global-stage' requires the baseline or a batch flow, "
-                           f"got {c.flow_id!r}")
-        units = REALIZATION_UNITS.get(real, ())
-        if units and c.processing_unit not in units:
-            reasons.append(f"processing-unit: realization {real!r} lowers only as {', '.join(units)}; "
-                           f"got {c.processing_unit!r}")
-        res = REALIZATION_LOCAL_RESIDENCES.get(real, ())
-        if res and local_res not in res:
-            reasons.append(f"local_residence: realization {real!r} evidences only {', '.join(res)}; "
-                           f"got {local_res!r}")
-        if real == "grouped-boundary" and c.glog < 1:
-            reasons.append(f"glog: realization 'grouped-boundary' needs glog >= 1, got {c.glog}")
-
-    if c.fused_tile > 1 and not _is_local(c.flow_id):
-        reasons.append(f"flow_id: fused_tile={c.fused_tile} requires flow 'local-fused-tile', got {c.flow_id!r}")
-    if c.fused_tile == 1 and not _is_global(c.flow_id):
-        reasons.append(f"flow_id: fused_tile=1 requires flow 'baseline-global-stage' or a batch flow, "
-                       f"got {c.flow_id!r}")
-
-    if c.batch_variant == "none":
-        if c.batch != 1:
-            reasons.append(f"batch: batch={c.batch} needs a batch variant ('spread'/'folded'); "
-                           "got batch_variant='none'")
-        if c.flow_id in ("batch-spread", "batch-folded"):
-            reasons.append(f"flow_id: {c.flow_id!r} requires batch_variant "
-                           f"'{c.flow_id.removeprefix('batch-')}', got 'none'")
-        if c.ud != 1 or c.td != 1:
-            reasons.append(f"data expansion: Ud/Td != 1 is lowered only through a batch variant; "
-                           f"got Ud={c.ud}, Td={c.td}")
-    else:
-        if c.batch_variant not in ("spread", "folded"):
-            reasons.append(f"batch_variant: must be 'none'/'spread'/'folded', got {c.batch_variant!r}")
-            return Verdict(c, LoweringStatus.NOT_LOWERED, tuple(reasons))
-        if c.batch <= 0 or (c.batch & (c.batch - 1)) != 0:
-            reasons.append(f"batch: must be a power of two, got {c.batch}")
-        if c.batch_variant == "spread":
-            if real == "matrix-resident":
-                if not _is_local(c.flow_id):
-                    reasons.append(f"flow_id: matrix-resident batch keeps 'local-fused-tile', got {c.flow_id!r}")
-            elif not (c.flow_id in _BATCH_SPREAD_FLOWS or c.flow_id in SPECIALIZED_ROUTING):
-                reasons.append(f"flow_id: spread variant requires 'batch-spread' for {real!r}, got {c.flow_id!r}")
-            if c.ud != c.batch or c.td != 1:
-                reasons.append(f"data expansion: spread requires Ud=batch={c.batch}, Td=1; "
-                               f"got Ud={c.ud}, Td={c.td}")
-        else:
-            if real != "global-stage" or c.processing_unit != "radix2-scalar":
-                reasons.append(f"batch_variant: folded (Td) lowers the M4 radix-2 stage cascade only; "
-                               f"{real}/{c.processing_unit} folded is not-lowered")
-            elif c.flow_id != "batch-folded":
-                reasons.append(f"flow_id: folded variant requires 'batch-folded', got {c.flow_id!r}")
-            if c.ud != 1 or c.td != c.batch:
-                reasons.append(f"data expansion: folded requires Ud=1, Td=batch={c.batch}; "
-                               f"got Ud={c.ud}, Td={c.td}")
-        if c.fused_tile > 1 and not (real == "matrix-resident" and c.batch_variant == "spread"):
-            reasons.append(f"fused_tile: batched paths consume fused_tile only for the matrix-resident "
-                           f"spread lowering; got fused_tile={c.fused_tile}")
-
-    if c.pipeline != "none":
-        reasons.append(f"pipeline: {c.pipeline!r} is not-lowered (no overlap evidence)")
-
-    status = LoweringStatus.NOT_LOWERED if reasons else LoweringStatus.LEGAL
-    return Verdict(c, status, tuple(reasons))
+    """Run every rule; the candidate is legal when none objects."""
+    low = LOWERINGS.get(effective_flow_realization(c))
+    reasons = tuple(r for rule in RULES for r in rule(c, low))
+    return Verdict(c, LoweringStatus.NOT_LOWERED if reasons else LoweringStatus.LEGAL, reasons)

@@ -19,7 +19,7 @@ import torch
 import torch.multiprocessing as mp
 
 from bfft import _lib, dist as bdist
-from bfft.entry import ExecutionPlan, execute_fft_plan
+from bfft.entry import ExecutionPlan, execute_fft_plan, native_plan_for
 from bfft.error_metric import rel_l2_per_transform
 from oracle import dist_oracle
 
@@ -235,12 +235,24 @@ def _dft_bins_f64(x: torch.Tensor, bins, chunk=1 << 26):
     return np.array(out)
 
 
-def test_config5b_single_gpu_n2p30():
+@pytest.mark.parametrize("which", ["bench-plan", "tile-1024"])
+def test_config5b_single_gpu_n2p30(which):
+    """N = 2^30 on one GPU: the plan bench.py times for config 5b (a 128-point
+    local group and three tail passes: 7 + 8 + 8 + 7 stages, three-level W_N
+    twiddles in the column passes), and a 1024-point local group."""
     n = 1 << 30
     g = torch.Generator(device=DEV).manual_seed(2030)
     x = torch.complex(torch.randn(n, device=DEV, generator=g), torch.randn(n, device=DEV, generator=g))
-    base = dict(n=n, batch=1, direction="dit", precision="fp32", selection_source="table", reason="t",
-                fallback=False, executed="fft_dit_matrix", block=256, params={"tile": 1024})
+    if which == "bench-plan":
+        import bench
+
+        plan, _ = bench.choose_plan(n, 1)
+        assert plan.executed == "fft_dit_matrix" and plan.params["tile"] == 128, plan
+        assert native_plan_for(plan, 0).launches == 4
+        base = {k: v for k, v in plan.__dict__.items() if k not in ("transform_direction",)}
+    else:
+        base = dict(n=n, batch=1, direction="dit", precision="fp32", selection_source="table", reason="t",
+                    fallback=False, executed="fft_dit_matrix", block=256, params={"tile": 1024})
     fwd = ExecutionPlan(**base)
     y = execute_fft_plan(fwd, x)
     rng = np.random.default_rng(7)

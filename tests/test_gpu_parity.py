@@ -238,6 +238,56 @@ def test_real_flows(n, b, norm, dedicated):
     assert rel_l2_per_transform(r, ref) <= TOL_F64, ("c2r", n, b, norm, dedicated)
 
 
+@pytest.mark.parametrize("n", [4096, 16384, 65536])
+@pytest.mark.parametrize("flow", ["product", "dedicated", "compat"])
+def test_config4_full_shape(n, flow):
+    """Config 4 at its exact shape (B = 256): the plan bench.py times
+    ("product": the selector's choice, or the explicit dedicated flow when it
+    abstains), the dedicated flow with a 256-point local group, and the packed
+    C2C compat flow; every row against float64."""
+    import bench
+
+    b = 256
+    rng = np.random.default_rng(n)
+    x = rng.standard_normal((b, n)).astype(np.float32)
+    xh = np.fft.rfft(rng.standard_normal((b, n)).astype(np.float32).astype(np.float64)).astype(np.complex64)
+    for tt, td, inp in (("r2c", "forward", x), ("c2r", "inverse", xh)):
+        if flow == "product":
+            p, _ = bench.choose_plan(n, b, tt, td)
+        else:
+            rf = "dedicated-r2c-pack-v1" if tt == "r2c" else "dedicated-c2r-hermitian-v1"
+            params = {"real_flow": rf} if flow == "dedicated" else {"real_compat": "packed-c2c-compat"}
+            params.update(tile=256, batch=b, variant="spread")
+            p = _plan("fft_dit_matrix_batch", n, b, transform_type=tt, transform_direction=td, params=params)
+        got = host(execute_fft_plan(p, dev(inp)))
+        if tt == "r2c":
+            ref = np.fft.rfft(inp.astype(np.float64), axis=-1)
+        else:
+            ref = np.fft.irfft(inp.astype(np.complex128), n=n, axis=-1)
+        assert got.shape == ref.shape, (tt, got.shape)
+        assert rel_l2_per_transform(got, ref) <= TOL_F64, (tt, flow, p.executed, p.params)
+
+
+@pytest.mark.parametrize("n", [1024, 2048])
+def test_config2_full_shape(n):
+    """Config 2 at B = 64: forward, inverse (1/N) and the round trip through
+    the plans bench.py times, every row against float64."""
+    import bench
+
+    b = 64
+    rng = np.random.default_rng(n + 64)
+    x = cplx(rng, (b, n))
+    pf, _ = bench.choose_plan(n, b, "c2c", "forward")
+    pi, _ = bench.choose_plan(n, b, "c2c", "inverse")
+    t = dev(x)
+    y = execute_fft_plan(pf, t)
+    back = execute_fft_plan(pi, y)
+    x64 = x.astype(np.complex128)
+    assert rel_l2_per_transform(host(y), np.fft.fft(x64, axis=-1)) <= TOL_F64
+    assert rel_l2_per_transform(host(execute_fft_plan(pi, t)), np.fft.ifft(x64, axis=-1)) <= TOL_F64
+    assert rel_l2_per_transform(host(back), x64) <= 2 * TOL_F64
+
+
 def test_run_fft_public_api_and_squeeze():
     rng = np.random.default_rng(4)
     x = cplx(rng, (1, 2048))

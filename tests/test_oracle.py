@@ -166,3 +166,42 @@ def test_hybrid_restatement_is_a_dft():
 
 def test_rel_l2_is_nan_safe():
     assert O.rel_l2(np.array([np.nan]), np.array([1.0])) == float("inf")
+
+
+def test_oracle_matches_the_reference_rows_at_baseline_shapes():
+    """The row-subset fixture (the reference's output on the first rows of
+    configurations 2, 3, 4 and 5a, tests/golden/make_golden_rows.py) pins the
+    oracle at the BASELINE shapes too; the fixture itself is a transform
+    (float64 check at its sampled positions)."""
+    import json
+    import os
+
+    from conftest import GOLDEN_DIR
+    from golden import row_cases
+
+    with open(os.path.join(GOLDEN_DIR, "reference_rows.json")) as f:
+        meta = json.load(f)["cases"]
+    rows = np.load(os.path.join(GOLDEN_DIR, "reference_rows.npz"))
+    assert {m["config"] for m in meta.values()} >= {"2", "3", "4", "5a"}
+    for case in row_cases.CASES:
+        lab = case["label"]
+        if lab not in meta:
+            continue
+        x = row_cases.case_input(case)
+        pos, want = rows[lab + "__pos"], rows[lab + "__out"]
+        if case["ref"] == "plan":
+            got = O.execute(case["executed"], x, case["tt"], case["td"], "backward",
+                            case["params"].get("real_flow"), case["params"])
+        else:
+            got = O.core_fft(case["ref"], x, case["knobs"])
+        assert list(got.shape) == meta[lab]["out_shape"], lab
+        e = O.rel_l2(got.reshape(-1)[pos], want)
+        assert e <= TOL_VS_REF, (lab, e)
+        if case["tt"] == "c2c":
+            x64 = x.astype(np.complex128)
+            ref64 = np.fft.fft(x64, axis=-1) if case["td"] == "forward" else np.fft.ifft(x64, axis=-1)
+        elif case["tt"] == "r2c":
+            ref64 = np.fft.rfft(x.astype(np.float64), axis=-1)
+        else:
+            ref64 = np.fft.irfft(x.astype(np.complex128), n=case["n"], axis=-1)
+        assert O.rel_l2(want, ref64.reshape(-1)[pos]) <= 1e-6, lab
