@@ -70,7 +70,11 @@ double norm_scale(int64_t n, int tdir, int norm) {
     return 1.0;
 }
 
-enum StepKind { S_STAGE2, S_STAGE4, S_PASS, S_CLUSTER };
+enum StepKind { S_STAGE2, S_STAGE4, S_PASS, S_CLUSTER, S_FUSED };
+
+// A local group of the whole transform (2^13 .. 2^16 points) runs as the fused
+// single-pass kernel from this batch on, as the cluster kernel below it.
+constexpr int64_t kFusedMinBatch = 2;
 
 struct Step {
     StepKind kind;
@@ -78,6 +82,7 @@ struct Step {
     StageArgs st{};
     PassArgs pa{};
     ClusterArgs ca{};
+    FusedArgs fa{};
     int log2l = 0, layout = 0, lmap = 0, smap = 0;
     int block = 256;
 };
@@ -96,6 +101,8 @@ struct bfft_plan_s {
     TwAlloc twc, twf;        // W_core and (real flows) W_N
     std::vector<Step> core;  // unnormalised forward core on (batch, core_n)
     size_t ws_bytes = 0;
+    size_t aux_offset = 0;   // start of the fused kernel's scratch ring in the workspace
+    bool has_aux = false;
     int launches = 0;
 };
 
@@ -430,6 +437,16 @@ bfft_status build_core(bfft_plan_s& P) {
             if (lt > kMaxPassLog2) {
                 // A local group of the whole transform beyond one CTA: the
                 // cluster kernel holds all N points on chip across its CTAs.
+                if (lt == log2n && fused_supported(log2n) && B >= kFusedMinBatch) {
+                    Step f;
+                    f.kind = S_FUSED;
+                    f.log2l = log2n;
+                    f.fa.batch = B;
+                    f.fa.tw = tw;
+                    f.fa.scale = 1.0f;
+                    st.push_back(f);
+                    return BFFT_OK;
+                }
                 if (lt == log2n && cluster_supported(log2n)) {
                     Step c;
                     c.kind = S_CLUSTER;
@@ -516,6 +533,7 @@ bfft_status build_core(bfft_plan_s& P) {
 void set_first_conj(Step& s) {
     if (s.kind == S_PASS) s.pa.conj_in = 1;
     else if (s.kind == S_CLUSTER) s.ca.conj_in = 1;
+    else if (s.kind == S_FUSED) s.fa.conj_in = 1;
     else s.st.conj_in = 1;
 }
 void set_last_epilogue(Step& s, int conj, float scale) {
@@ -525,6 +543,9 @@ void set_last_epilogue(Step& s, int conj, float scale) {
     } else if (s.kind == S_CLUSTER) {
         s.ca.conj_out = conj;
         s.ca.scale = scale;
+    } else if (s.kind == S_FUSED) {
+        s.fa.conj_out = conj;
+        s.fa.scale = scale;
     } else {
         s.st.conj_out = conj;
         s.st.scale = scale;
@@ -533,7 +554,8 @@ void set_last_epilogue(Step& s, int conj, float scale) {
 
 // after_pass: the previous kernel on the stream is a pass of this flow, so a
 // TMA pass may be launched as its programmatic dependent.
-cudaError_t launch_step(const Step& s, const float2* in, float2* out, cudaStream_t stream, bool after_pass = false) {
+cudaError_t launch_step(const Step& s, const float2* in, float2* out, cudaStream_t stream, bool after_pass = false,
+                        void* aux = nullptr) {
     g_launches.fetch_add(1, std::memory_order_relaxed);
     switch (s.kind) {
         case S_STAGE2: return launch_radix2_stage(s.dif, in, out, s.st, s.block, stream);
@@ -544,6 +566,18 @@ cudaError_t launch_step(const Step& s, const float2* in, float2* out, cudaStream
             return launch_pass(s.log2l, s.layout, s.lmap, s.smap, in, out, pa, stream);
         }
         case S_CLUSTER: return launch_cluster_fft(s.log2l, in, out, s.ca, stream);
+        case S_FUSED: {
+            // TMA needs 16-byte aligned buffers; otherwise the cluster kernel runs the same transform
+            const cudaError_t e = aux ? launch_fused_fft(s.log2l, in, out, aux, s.fa, stream) : cudaErrorNotSupported;
+            if (e != cudaErrorNotSupported) return e;
+            ClusterArgs c{};
+            c.batch = s.fa.batch;
+            c.tw = s.fa.tw;
+            c.scale = s.fa.scale;
+            c.conj_in = s.fa.conj_in;
+            c.conj_out = s.fa.conj_out;
+            return launch_cluster_fft(s.log2l, in, out, c, stream);
+        }
         default: return cudaErrorInvalidValue;
     }
 }
@@ -551,11 +585,11 @@ cudaError_t launch_step(const Step& s, const float2* in, float2* out, cudaStream
 // Runs the core steps from `src` into `dst`, ping-ponging through `scratch`;
 // neither `src` nor its aliases are ever written.
 cudaError_t run_core(const Step* st, size_t L, const float2* src, float2* dst, float2* scratch,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, void* aux = nullptr) {
     const float2* cur = src;
     for (size_t i = 0; i < L; ++i) {
         float2* tgt = ((L - 1 - i) % 2 == 0) ? dst : scratch;
-        cudaError_t e = launch_step(st[i], cur, tgt, stream, i > 0 && st[i - 1].kind == S_PASS);
+        cudaError_t e = launch_step(st[i], cur, tgt, stream, i > 0 && st[i - 1].kind == S_PASS, aux);
         if (e != cudaSuccess) return e;
         cur = tgt;
     }
@@ -671,6 +705,12 @@ bfft_status bfft_plan_create(const bfft_plan_desc* desc, bfft_plan_t* plan) {
         P->ws_bytes = 3 * sizeof(float2) * (size_t)(B * n);
         P->launches = (L == 0 ? 1 : L) + 2;
     }
+    for (const Step& stp : P->core)
+        if (stp.kind == S_FUSED) P->has_aux = true;
+    if (P->has_aux) {  // the fused kernel's L2-resident scratch ring follows the flow's buffers
+        P->aux_offset = (P->ws_bytes + 255) & ~(size_t)255;
+        P->ws_bytes = P->aux_offset + fused_workspace_bytes(c, B);
+    }
     *plan = P;
     return BFFT_OK;
 }
@@ -717,6 +757,7 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
     cudaError_t e = cudaSuccess;
     std::vector<Step> core = plan->core;  // epilogue flags are per call
     float2* ws = static_cast<float2*>(workspace);
+    void* aux = plan->has_aux ? static_cast<void*>(static_cast<unsigned char*>(workspace) + plan->aux_offset) : nullptr;
 
     if (d.transform_type == BFFT_C2C) {
         const float scale = (float)norm_scale(n, d.transform_direction, d.norm);
@@ -726,7 +767,7 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
         } else {
             if (inverse) set_first_conj(core.front());
             set_last_epilogue(core.back(), inverse ? 1 : 0, scale);
-            e = run_core(core.data(), core.size(), (const float2*)in, (float2*)out, ws, s);
+            e = run_core(core.data(), core.size(), (const float2*)in, (float2*)out, ws, s, aux);
         }
     } else if (d.real_flow == BFFT_REAL_DEDICATED) {
         float2* F = ws;
@@ -735,7 +776,7 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
             // pack: the float32 (B, N) input IS the complex64 (B, N/2) z
             const float scale = (float)norm_scale(n, BFFT_FORWARD, d.norm);
             e = core.empty() ? launch_scale((const float2*)in, F, B * c, 1.0f, 0, s)
-                             : run_core(core.data(), core.size(), (const float2*)in, F, A, s);
+                             : run_core(core.data(), core.size(), (const float2*)in, F, A, s, aux);
             if (core.empty()) g_launches.fetch_add(1, std::memory_order_relaxed);
             if (e == cudaSuccess) {
                 g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -753,7 +794,7 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
                 // (float32 pairs = complex64 (B, N/2)) and the unpack pass goes away.
                 set_first_conj(core.front());
                 set_last_epilogue(core.back(), 1, scale);
-                e = run_core(core.data(), core.size(), C, (float2*)out, A, s);
+                e = run_core(core.data(), core.size(), C, (float2*)out, A, s, aux);
             } else if (e == cudaSuccess) {
                 g_launches.fetch_add(2, std::memory_order_relaxed);
                 e = launch_scale(C, F, B * c, 1.0f, 0, s);
@@ -769,7 +810,7 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
             g_launches.fetch_add(1, std::memory_order_relaxed);
             e = launch_real_to_complex((const float*)in, C, B * n, s);
             if (e == cudaSuccess) {
-                e = core.empty() ? launch_scale(C, F, B * n, 1.0f, 0, s) : run_core(core.data(), core.size(), C, F, A, s);
+                e = core.empty() ? launch_scale(C, F, B * n, 1.0f, 0, s) : run_core(core.data(), core.size(), C, F, A, s, aux);
                 if (core.empty()) g_launches.fetch_add(1, std::memory_order_relaxed);
             }
             if (e == cudaSuccess) {
@@ -781,7 +822,7 @@ bfft_status bfft_execute(bfft_plan_t plan, const void* in, void* out, void* work
             g_launches.fetch_add(1, std::memory_order_relaxed);
             e = launch_hermitian_conj((const float2*)in, C, n, B, s);
             if (e == cudaSuccess) {
-                e = core.empty() ? launch_scale(C, F, B * n, 1.0f, 0, s) : run_core(core.data(), core.size(), C, F, A, s);
+                e = core.empty() ? launch_scale(C, F, B * n, 1.0f, 0, s) : run_core(core.data(), core.size(), C, F, A, s, aux);
                 if (core.empty()) g_launches.fetch_add(1, std::memory_order_relaxed);
             }
             if (e == cudaSuccess) {

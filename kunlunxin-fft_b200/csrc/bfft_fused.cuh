@@ -1,0 +1,498 @@
+// bfft_fused.cuh -- whole transforms of N = N1 * N2 points (2^13 .. 2^16) in
+// one HBM round trip, as one persistent kernel.
+//
+// Included by bfft_kernels.cu after bfft_pass_tma.cuh (it uses the TMA /
+// mbarrier helpers, the Stockham passes and the column-tile geometry).
+//
+// The 4-step decomposition X[k1 + N1 k2] = sum_n2 W_N2^{n2 k2} W_N^{n2 k1}
+// sum_n1 x[n1 N2 + n2] W_N1^{n1 k1} splits every transform into
+//   phase A: N2 column FFTs of N1 points (x read with stride N2), the twiddle
+//            W_N^{k1 n2} applied to their outputs, each column's N1 outputs
+//            written as one row n2 of a scratch slot S[n2][k1];
+//   phase B: N1 FFTs of N2 points over n2 for each k1 (columns of S), written
+//            to X[k1 + N1 k2] (out read as [k2][k1], k1 contiguous).
+// Both phases are tiles of K = 16 (or more, for short sub-FFTs) sub-FFTs
+// loaded by one TMA box into a dense [element][sub-FFT] shared tile -- the
+// column-pass geometry (PassTGeo) -- so the same tile is the landing buffer,
+// the Stockham exchange area and the store staging.
+//
+// The intermediate never goes to HBM on purpose: scratch slots form a ring of
+// S transforms (tens of MiB) whose stores and loads carry an L2 evict_last
+// policy while the input and output streams carry evict_first, so the ring
+// stays in the 126 MB L2 and HBM sees one read of x and one write of X.
+//
+// Scheduling: tickets from one global counter, in rounds of TA + TB tickets:
+// round r holds the TA phase-A tiles of transform r and the TB phase-B tiles
+// of transform r - D (the lag D lets phase A of a transform finish before its
+// phase-B tickets come up).  Dependencies point only to earlier tickets:
+//   B(b, i) needs the TA phase-A tiles of b completed (a_done[slot]);
+//   A(b, j) needs the TB phase-B tiles of b - S (the slot's previous user)
+//           to have read the slot (b_done[slot]), and S > D.
+// A CTA processes its tickets in order and claims the next one while working
+// on the current one, so the smallest unfinished ticket can always proceed:
+// no co-residency is assumed.  Every wait is bounded (kWaitLimitNs of
+// %globaltimer); an expired wait sets bit 1 (dependency) or bit 0 (mbarrier)
+// of bfft_device_status and the CTA stops after its copies in flight land.
+#pragma once
+
+namespace bfft {
+
+template <int LA, int LB>
+struct FusedGeo {
+    using GA = PassTGeo<LA, 1>;  // phase A: column FFTs of N1, rows out (bulk copies)
+    using GB = PassTGeo<LB, 0>;  // phase B: column FFTs of N2 over the slot, columns out (TMA store)
+    static constexpr int N1 = 1 << LA, N2 = 1 << LB;
+    static constexpr int CONSUMERS = 256;
+    static constexpr int THREADS = CONSUMERS + 64;  // + the loader and the storer warps
+    static_assert(GA::THREADS == CONSUMERS && GB::THREADS == CONSUMERS, "256-thread column tiles");
+    static constexpr int SB = GA::SB > GB::SB ? GA::SB : GB::SB;
+    static constexpr int STAGES = 3;
+    static constexpr int TA = N2 / GA::K;  // phase-A tiles per transform
+    static constexpr int TB = N1 / GB::K;  // phase-B tiles per transform
+    static_assert(TA >= 1 && TB >= 1, "N1 * N2 >= 4096");
+    static constexpr int TWA = tw_total(LA), TWB = tw_total(LB);
+    // alignment slack, stages, control block (mbarriers, the stage items), tables; no static
+    // shared memory, so the launcher may raise the dynamic limit to the full 227 KiB
+    static constexpr int CTRL = 256;
+    static constexpr size_t SMEM =
+        128 + (size_t)STAGES * SB + CTRL + (size_t)(TWA + TWB + GA::COLTW_ENTRIES) * sizeof(float2);
+};
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                                 uint64_t* bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+__device__ __forceinline__ void tma_store_3d_hint(const CUtensorMap* map, int c0, int c1, int c2, const void* src,
+                                                  uint64_t pol) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group.L2::cache_hint"
+                 " [%0, {%1, %2, %3}], [%4], %5;" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src)), "l"(pol)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_store_hint(void* dst, const void* src, uint32_t bytes, uint64_t pol) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group.L2::cache_hint [%0], [%1], %2, %3;" ::"l"(
+                     reinterpret_cast<uint64_t>(dst)),
+                 "r"(smem_u32(src)), "r"(bytes), "l"(pol)
+                 : "memory");
+}
+// Order this thread's generic-proxy accesses (an acquire just made) with its
+// later async-proxy (TMA / bulk) accesses of global memory, and the reverse.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Wait (bounded) until *p >= target; false and status bit 1 on expiry.
+__device__ __forceinline__ bool counter_wait_bounded(const uint32_t* p, uint32_t target) {
+    if (ld_acquire_u32(p) >= target) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+        __nanosleep(64);
+        if (ld_acquire_u32(p) >= target) return true;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(&g_kernel_status, 2u);
+            return false;
+        }
+    }
+}
+
+// One claimed work item.  kind: 0 none (no tickets left), 1 phase A, 2 phase B.
+struct FusedItem {
+    int kind;
+    int idx;      // tile within the phase
+    int64_t b;    // transform
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+
+// Warp-specialised: warps 0-7 (the consumers) compute tiles and meet only at
+// named barrier 1; lane 0 of warp 8 (the loader) claims tickets, waits on
+// dependencies and starts the TMA loads; lane 0 of warp 9 (the storer) stores
+// finished tiles and publishes them.  Consumers never wait for a global
+// atomic or a store to complete.  The q-th item of the CTA uses stage q % ST:
+//   full[s]   loader    -> consumers, storer: the tile landed (s_item[s] set);
+//   staged[s] consumers -> storer: the results are staged in the stage;
+//   empty[s]  storer    -> loader: the stores have read the stage.
+// The storer publishes a phase-A tile (a_done) as soon as its row stores are
+// complete (after releasing the stage), a phase-B tile (b_done) as soon as it
+// has landed.  An issued item therefore finishes without the
+// loader, and the loader may block on a dependency (always an earlier ticket)
+// without closing a cycle.
+template <int LA, int LB>
+__global__ void __launch_bounds__(FusedGeo<LA, LB>::THREADS, 2)
+    k_fused_fft(const __grid_constant__ CUtensorMap ta_in, const __grid_constant__ CUtensorMap tb_in,
+                const __grid_constant__ CUtensorMap tb_out, FusedArgs a) {
+    using G = FusedGeo<LA, LB>;
+    using GA = typename G::GA;
+    using GB = typename G::GB;
+    constexpr int ST = G::STAGES;
+    constexpr int NC = G::CONSUMERS;
+    static_assert(8 * 3 * ST + ST * sizeof(FusedItem) + sizeof(int) <= G::CTRL, "control block");
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* base =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    unsigned char* ctrl = base + ST * G::SB;
+    uint64_t* full = reinterpret_cast<uint64_t*>(ctrl);
+    uint64_t* staged = full + ST;
+    uint64_t* empty = staged + ST;
+    FusedItem* s_item = reinterpret_cast<FusedItem*>(ctrl + 8 * 3 * ST);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(ctrl + 8 * 3 * ST + ST * sizeof(FusedItem));
+    float2* twA = reinterpret_cast<float2*>(ctrl + G::CTRL);
+    float2* twB = twA + G::TWA;
+    float2* coltw = twB + G::TWB;
+    auto stage = [&](int s) { return reinterpret_cast<float2*>(base + s * G::SB); };
+
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&staged[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_proxy_async_smem();
+        *s_abort = 0;
+    }
+    fill_stockham_twiddles<LA>(twA);
+    fill_stockham_twiddles<LB>(twB);
+    SmemTwiddle<2> twiddle;  // W_N lookups (phase-A post-twiddle), staged in shared memory when they fit
+    {
+        PassArgs pa{};
+        pa.tw = a.tw;
+        pa.tw_smem_entries = a.tw_smem_entries;
+        pa.tw_smem_levels = a.tw_smem_levels;
+        twiddle.setup(coltw + GA::COLTW_ENTRIES, pa);
+    }
+    __syncthreads();  // the last CTA-wide barrier: the warps part ways here
+
+    const int S = a.slots;
+    uint32_t* a_done = a.counters + 1;
+    uint32_t* b_done = a.counters + 1 + S;
+    if (tid == NC) {
+        // ================================================ loader
+        uint32_t* ticket = a.counters;
+        const int64_t round_len = G::TA + G::TB;
+        const int64_t ntickets = (a.batch + a.lag) * round_len;
+        const uint64_t pol_stream = policy_evict_first(), pol_keep = policy_evict_last();
+        griddep_wait();
+        auto decode = [&](uint32_t t) -> FusedItem {  // kind -1: a ticket of no work (ring edges)
+            if ((int64_t)t >= ntickets) return FusedItem{0, 0, 0};
+            const int64_t r = (int64_t)t / round_len;
+            const int j = (int)((int64_t)t - r * round_len);
+            if (j < G::TA) return r < a.batch ? FusedItem{1, j, r} : FusedItem{-1, 0, 0};
+            return (r >= a.lag && r - a.lag < a.batch) ? FusedItem{2, j - G::TA, r - a.lag} : FusedItem{-1, 0, 0};
+        };
+        auto ready = [&](const FusedItem& it, bool block) -> bool {
+            const int slot = (int)(it.b % S);
+            const uint32_t gen = (uint32_t)(it.b / S);
+            const uint32_t* p = it.kind == 1 ? b_done + slot : a_done + slot;
+            const uint32_t target = it.kind == 1 ? gen * (uint32_t)G::TB : (gen + 1) * (uint32_t)G::TA;
+            return block ? counter_wait_bounded(p, target) : ld_acquire_u32(p) >= target;
+        };
+        bool failed = false;
+        uint32_t next_ticket = atomicAdd(ticket, 1u);
+        int64_t q = 0;
+        for (;; ++q) {
+            FusedItem nx = decode(next_ticket);
+            while (nx.kind < 0) nx = decode(atomicAdd(ticket, 1u));
+            if (nx.kind == 0) break;
+            next_ticket = atomicAdd(ticket, 1u);  // the next claim's latency hides behind this item
+            const int s = (int)(q % ST);
+            if (q >= ST && !mbar_wait_bounded(&empty[s], (uint32_t)(((q - ST) / ST) & 1))) {
+                failed = true;
+                break;
+            }
+            // Items already issued finish without the loader (consumers compute them, the
+            // storer stores and publishes them, flushing before it blocks), so blocking here
+            // cannot close a cycle: every dependency is an earlier ticket.
+            if (!ready(nx, true)) {
+                failed = true;
+                break;
+            }
+            s_item[s] = nx;
+            fence_proxy_async_global();
+            float2* dst = stage(s);
+            if (nx.kind == 1) {
+                mbar_arrive_expect_tx(&full[s], (uint32_t)(GA::K * GA::L * sizeof(float2)));
+#pragma unroll
+                for (int j = 0; j < GA::L / GA::LB; ++j)
+                    tma_load_3d_hint(dst + j * GA::LB * GA::K, &ta_in, nx.idx * GA::K, j * GA::LB, (int)nx.b,
+                                     &full[s], pol_stream);
+            } else {
+                mbar_arrive_expect_tx(&full[s], (uint32_t)(GB::K * GB::L * sizeof(float2)));
+#pragma unroll
+                for (int j = 0; j < GB::L / GB::LB; ++j)
+                    tma_load_3d_hint(dst + j * GB::LB * GB::K, &tb_in, nx.idx * GB::K, j * GB::LB,
+                                     (int)(nx.b % S), &full[s], pol_keep);
+            }
+            if (*s_abort) {
+                ++q;
+                failed = true;
+                break;
+            }
+        }
+        if (failed) {
+            *s_abort = 1;
+            atomicOr(&g_kernel_status, 2u);
+        }
+        // the end item, in the next stage once it is free
+        const int s = (int)(q % ST);
+        if (q < ST || mbar_wait_bounded(&empty[s], (uint32_t)(((q - ST) / ST) & 1))) {
+            s_item[s] = FusedItem{0, 0, 0};
+            mbar_arrive(&full[s]);
+        }
+        // loads this CTA started land before it leaves (bounded); item q - ST's stage holds the end item
+        for (int64_t r = q - ST + 1 > 0 ? q - ST + 1 : 0; r < q; ++r)
+            mbar_wait_bounded(&full[r % ST], (uint32_t)((r / ST) & 1));
+        return;
+    }
+    if (tid == NC + 32) {
+        // ================================================ storer
+        const uint64_t pol_stream = policy_evict_first(), pol_keep = policy_evict_last();
+        // phase-A slots whose row stores were committed but not yet published, oldest first
+        int pend[4];
+        int npend = 0;
+        auto publish = [&](bool all) {  // all: every pending group; else all but the newest group
+            if (npend == 0 || (!all && npend == 1)) return;
+            if (all) bulk_wait<0>();
+            else bulk_wait<1>();
+            fence_proxy_async_global();
+            const int n = all ? npend : npend - 1;
+            for (int i = 0; i < n; ++i) red_release_add(a_done + pend[i], 1u);
+            for (int i = n; i < npend; ++i) pend[i - n] = pend[i];
+            npend -= n;
+        };
+        // wait for a phase; before blocking, publish everything pending (another CTA may wait on it)
+        auto wait_phase = [&](uint64_t* bar, uint32_t par) -> bool {
+            if (mbar_try_wait(bar, par)) return true;
+            publish(true);
+            return mbar_wait_bounded(bar, par);
+        };
+        for (int64_t q = 0;; ++q) {
+            const int s = (int)(q % ST);
+            const uint32_t par = (uint32_t)((q / ST) & 1);
+            if (!wait_phase(&full[s], par)) {
+                *s_abort = 1;
+                break;
+            }
+            const FusedItem it = s_item[s];
+            if (it.kind == 0) break;
+            const int slot = (int)(it.b % S);
+            if (it.kind == 2) red_release_add(b_done + slot, 1u);  // its tile has left the slot
+            if (!wait_phase(&staged[s], par)) {
+                *s_abort = 1;
+                break;
+            }
+            float2* buf = stage(s);
+            if (it.kind == 1) {
+                float2* dst = a.scratch + (int64_t)slot * (G::N1 * G::N2) + (int64_t)(it.idx * GA::K) * G::N1;
+#pragma unroll 1
+                for (int r = 0; r < GA::K; ++r)
+                    bulk_store_hint(dst + (int64_t)r * G::N1, buf + r * (GA::L + GA::RPAD),
+                                    (uint32_t)(GA::L * sizeof(float2)), pol_keep);
+                bulk_commit();
+                pend[npend++] = slot;
+            } else {
+                const int c0 = it.idx * GB::K;
+#pragma unroll
+                for (int j = 0; j < GB::L / GB::LB; ++j)
+                    tma_store_3d_hint(&tb_out, c0, j * GB::LB, (int)it.b, buf + j * GB::LB * GB::K, pol_stream);
+                bulk_commit();
+            }
+            bulk_wait_read<0>();  // the stage may be refilled
+            mbar_arrive(&empty[s]);
+            publish(true);        // phase B of that transform may be waiting for these rows
+        }
+        publish(true);
+        bulk_wait<0>();
+        return;
+    }
+    if (tid >= NC) return;
+
+    // ==================================================== consumers (256 threads)
+    const float osr = a.scale, osi = a.conj_out ? -a.scale : a.scale;
+    const bool scaled = a.scale != 1.0f || a.conj_out;
+    for (int64_t q = 0;; ++q) {
+        const int s = (int)(q % ST);
+        const bool ok = mbar_wait_bounded(&full[s], (uint32_t)((q / ST) & 1));
+        if (!ok) *s_abort = 1;
+        group_sync<NC>();
+        const FusedItem cur = s_item[s];
+        if (cur.kind == 0 || *s_abort) break;
+        float2* buf = stage(s);
+        if (cur.kind == 1) {
+            // ---------------- phase A: column FFTs of N1, post-twiddle W_N^{k1 n2}, staged as rows
+            const int cl = tid % GA::K, t = tid / GA::K;
+            const uint32_t n2 = (uint32_t)(cur.idx * GA::K + cl);
+            float2 tb = make_float2(1.f, 0.f);
+            if constexpr (GA::COLTW) {
+#pragma unroll
+                for (int j = 0; j < GA::CPT; ++j) {
+                    const int m = t + j * GA::TF;
+                    if (m < 16) coltw[m * GA::K + cl] = twiddle(static_cast<uint32_t>(m * GA::TF) * n2);
+                }
+                tb = twiddle(static_cast<uint32_t>(t) * n2);
+            }
+            float2 v[16];
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+                float2 val = buf[(t + m * GA::TF) * GA::K + cl];
+                if (a.conj_in) val.y = -val.y;
+                v[m] = val;
+            }
+            group_sync<NC>();  // the tile is now the exchange area; the column factors are published
+            stockham_passes<LA, 0, 16, GA::TF, GA::K, true, NC>(v, t, buf + cl, twA);
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+                const uint32_t k = static_cast<uint32_t>(t + m * GA::TF);
+                float2 w;
+                if constexpr (GA::COLTW) w = cmul(tb, coltw[m * GA::K + cl]);
+                else w = twiddle(k * n2);
+                buf[cl * (GA::L + GA::RPAD) + k] = cmul(v[m], w);
+            }
+        } else {
+            // ---------------- phase B: column FFTs of N2 over the slot, epilogue, staged as columns of X
+            const int cl = tid % GB::K, t = tid / GB::K;
+            float2 v[16];
+#pragma unroll
+            for (int m = 0; m < 16; ++m) v[m] = buf[(t + m * GB::TF) * GB::K + cl];
+            group_sync<NC>();
+            stockham_passes<LB, 0, 16, GB::TF, GB::K, true, NC>(v, t, buf + cl, twB);
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+                const float2 val = v[m];
+                buf[(t + m * GB::TF) * GB::K + cl] = scaled ? make_float2(val.x * osr, val.y * osi) : val;
+            }
+        }
+        fence_proxy_async_smem();
+        group_sync<NC>();  // staged; also: every consumer has read s_item[s] and the column factors
+        if (tid == 0) mbar_arrive(&staged[s]);
+    }
+}
+
+// ---- host side ----
+
+template <int LA, int LB>
+static cudaError_t launch_fused_t(const float2* in, float2* out, const FusedArgs& a0, cudaStream_t s) {
+    using G = FusedGeo<LA, LB>;
+    using GA = typename G::GA;
+    using GB = typename G::GB;
+    constexpr size_t kSmemCap = 227 * 1024;
+    static std::atomic<int> blocks_per_sm[64][kTwClasses];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    const uint64_t N1 = G::N1, N2 = G::N2, N = N1 * N2;
+    CUtensorMap ta_in, tb_in, tb_out;
+    // x as [b][n1][n2]: sub-FFT (column) index n2 fastest
+    if (!encode_map_3d(&ta_in, in, N2, N1, (uint64_t)a0.batch, N2 * 8, N * 8, GA::K, GA::LB)) return cudaErrorNotSupported;
+    // slots as [slot][n2][k1]: phase B's sub-FFT index k1 fastest, element n2
+    if (!encode_map_3d(&tb_in, a0.scratch, N1, N2, (uint64_t)a0.slots, N1 * 8, N * 8, GB::K, GB::LB))
+        return cudaErrorNotSupported;
+    // X as [b][k2][k1]
+    if (!encode_map_3d(&tb_out, out, N1, N2, (uint64_t)a0.batch, N1 * 8, N * 8, GB::K, GB::LB))
+        return cudaErrorNotSupported;
+    FusedArgs a = a0;
+    PassArgs pa{};
+    pa.tw = a.tw;
+    pa.tw_mode = 2;
+    int cls = 0;
+    choose_tw_staging(pa, G::SMEM, kSmemCap, cls);
+    a.tw_smem_entries = pa.tw_smem_entries;
+    a.tw_smem_levels = pa.tw_smem_levels;
+    auto kern = k_fused_fft<LA, LB>;
+    int sms = 0, nb = 0;
+    e = device_sm_count(dev, &sms);
+    if (e == cudaSuccess) e = cached_occupancy(blocks_per_sm[dev][cls], kern, G::THREADS, G::SMEM + tw_class_bytes(cls),
+                                               kSmemCap, &nb);
+    if (e != cudaSuccess) return e;
+    const int64_t items = a.batch * (G::TA + G::TB);
+    int64_t grid = (int64_t)nb * sms;
+    if (grid > items) grid = items;
+    if (grid < 1) grid = 1;
+    const size_t smem = G::SMEM + (size_t)a.tw_smem_entries * sizeof(float2);
+    e = cudaMemsetAsync(a.counters, 0, sizeof(uint32_t) * (1 + 2 * (size_t)a.slots), s);
+    if (e != cudaSuccess) return e;
+    return launch_maybe_pdl(kern, (unsigned)grid, G::THREADS, smem, s, 0, ta_in, tb_in, tb_out, a);
+}
+
+// Scratch ring sizing, in tickets (the tiles of one transform form one round
+// of TA + TB tickets; a ticket stands for 16 KiB of ring): phase-B tiles come
+// up kLagTickets after their transform's phase-A tiles, and a slot is reused
+// kSlackTickets after its phase-B tiles came up, so S > D.  Measured on B200
+// (N = 2^16, B = 8192; N = 2^13, B = 65536): lag/slack 768/768 leaves the
+// loaders blocked on dependencies (2.96 ms), 1024/1024 2.69 ms, 1536/1536
+// 2.56 ms (a 48 MiB ring), 2048/2048 2.82 ms and 3072/1536 2.98 ms -- the
+// larger rings no longer stay in L2.
+constexpr int kLagTickets = 1536, kSlackTickets = 1536;
+
+inline int fused_round_len(int log2n) {
+    switch (log2n) {
+        case 13: return FusedGeo<7, 6>::TA + FusedGeo<7, 6>::TB;
+        case 14: return FusedGeo<7, 7>::TA + FusedGeo<7, 7>::TB;
+        case 15: return FusedGeo<8, 7>::TA + FusedGeo<8, 7>::TB;
+        default: return FusedGeo<8, 8>::TA + FusedGeo<8, 8>::TB;
+    }
+}
+
+inline void fused_ring(int64_t n, int64_t batch, int* slots, int* lag) {
+    int log2n = 0;
+    while ((int64_t(1) << log2n) < n) ++log2n;
+    const int rl = fused_round_len(log2n);
+    const int D = (kLagTickets + rl - 1) / rl;
+    const int64_t want = D + (kSlackTickets + rl - 1) / rl;
+    *lag = D;
+    *slots = (int)(batch < want ? batch : want);  // batch <= S: no slot is reused
+}
+
+bool fused_supported(int log2n) { return log2n >= 13 && log2n <= 16; }
+
+size_t fused_workspace_bytes(int64_t n, int64_t batch) {
+    int slots = 0, lag = 0;
+    fused_ring(n, batch, &slots, &lag);
+    return (size_t)slots * (size_t)n * sizeof(float2) + 256 + sizeof(uint32_t) * (1 + 2 * (size_t)slots);
+}
+
+cudaError_t launch_fused_fft(int log2n, const float2* in, float2* out, void* workspace, const FusedArgs& a0,
+                             cudaStream_t s) {
+    FusedArgs a = a0;
+    const int64_t n = int64_t(1) << log2n;
+    fused_ring(n, a.batch, &a.slots, &a.lag);
+    a.scratch = static_cast<float2*>(workspace);
+    a.counters = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(workspace) +
+                                             (size_t)a.slots * (size_t)n * sizeof(float2) + 128);
+    if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(workspace)) & 15)
+        return cudaErrorNotSupported;
+    switch (log2n) {
+        case 13: return launch_fused_t<7, 6>(in, out, a, s);
+        case 14: return launch_fused_t<7, 7>(in, out, a, s);
+        case 15: return launch_fused_t<8, 7>(in, out, a, s);
+        case 16: return launch_fused_t<8, 8>(in, out, a, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace bfft

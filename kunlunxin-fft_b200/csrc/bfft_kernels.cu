@@ -532,7 +532,16 @@ __device__ __forceinline__ int xaddr(int i) {
     else return i * XS;
 }
 
-template <int LOG2L, int PASS, int E, int TF, int XS = 0, bool PK = false>
+// Barrier of the threads that share the exchange area: the whole CTA
+// (NBAR = 0), or the NBAR threads of named barrier 1 (warp-specialised
+// kernels whose other warps do not take part).
+template <int NBAR>
+__device__ __forceinline__ void group_sync() {
+    if constexpr (NBAR == 0) __syncthreads();
+    else asm volatile("bar.sync 1, %0;" ::"n"(NBAR) : "memory");
+}
+
+template <int LOG2L, int PASS, int E, int TF, int XS = 0, bool PK = false, int NBAR = 0>
 __device__ __forceinline__ void stockham_passes(float2 (&v)[E], int t, float2* region, const float2* tw_smem) {
     constexpr int NP = LOG2L <= 4 ? 1 : (LOG2L + 3) / 4;
     if constexpr (PASS < NP) {
@@ -570,11 +579,11 @@ __device__ __forceinline__ void stockham_passes(float2 (&v)[E], int t, float2* r
 #pragma unroll
                 for (int j = 0; j < R; ++j) region[xaddr<XS>(base + (j << LP))] = v[q + j * NB];
             }
-            __syncthreads();
+            group_sync<NBAR>();
 #pragma unroll
             for (int m = 0; m < E; ++m) v[m] = region[xaddr<XS>(t + m * TF)];
-            __syncthreads();
-            stockham_passes<LOG2L, PASS + 1, E, TF, XS, PK>(v, t, region, tw_smem);
+            group_sync<NBAR>();
+            stockham_passes<LOG2L, PASS + 1, E, TF, XS, PK, NBAR>(v, t, region, tw_smem);
         }
     }
 }
@@ -950,6 +959,7 @@ static cudaError_t launch_pass_l(int layout, int lmap, int smap, const float2* i
 }  // namespace bfft
 
 #include "bfft_pass_tma.cuh"
+#include "bfft_fused.cuh"
 
 namespace bfft {
 

@@ -65,6 +65,28 @@ struct ClusterArgs {
 bool cluster_supported(int log2n);
 cudaError_t launch_cluster_fft(int log2n, const float2* in, float2* out, const ClusterArgs& a, cudaStream_t s);
 
+// ---------------------------------------------------------------- fused single pass
+// Whole transforms of N = 2^13 .. 2^16 in one HBM round trip without
+// clusters: the 4-step's two phases as tiles of one persistent kernel, the
+// intermediate in an L2-resident ring of scratch slots (workspace).
+struct FusedArgs {
+    int64_t batch;
+    TwoLevel tw;              // the plan's W_N
+    float scale;
+    int conj_in, conj_out;
+    int tw_smem_entries, tw_smem_levels;  // set by the launcher
+    uint32_t* counters;       // [0] ticket, [1, 1+S) a_done, [1+S, 1+2S) b_done; zeroed before each launch
+    float2* scratch;          // S slots of N complex64
+    int slots;                // S (set by the launcher)
+    int lag;                  // D rounds (set by the launcher)
+    int pdl;
+};
+bool fused_supported(int log2n);
+// Workspace of one launch: the scratch ring and its counters.
+size_t fused_workspace_bytes(int64_t n, int64_t batch);
+cudaError_t launch_fused_fft(int log2n, const float2* in, float2* out, void* workspace, const FusedArgs& a,
+                             cudaStream_t s);
+
 // Status word the kernels set when a bounded wait expires (bit 0: an
 // mbarrier wait of the TMA pass); read synchronously, optionally cleared.
 cudaError_t read_device_status(unsigned* status, bool clear);

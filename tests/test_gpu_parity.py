@@ -378,20 +378,48 @@ def test_sweep_config_full_size_properties():
         del x, y, back, y2
 
 
-def test_batch_shard_config_full_size():
-    """Config 5a on one GPU: N=65536, B=8192 (4 GiB): round trip on device and
-    sampled rows against float64."""
+@pytest.mark.parametrize("tile", [256, 65536])
+def test_batch_shard_config_full_size(tile):
+    """Config 5a on one GPU: N=65536, B=8192 (4 GiB), as two passes (tile 256)
+    and as the fused single pass (tile = N): round trip on device and sampled
+    rows against float64."""
     n, b = 65536, 8192
     g = torch.Generator(device=DEV).manual_seed(99)
     x = torch.complex(torch.randn(b, n, device=DEV, generator=g), torch.randn(b, n, device=DEV, generator=g))
-    fwd = _plan("fft_dit_matrix_batch", n, b, params={"tile": 256})
+    fwd = _plan("fft_dit_matrix_batch", n, b, params={"tile": tile})
     y = execute_fft_plan(fwd, x)
     rows = [0, 1, 4095, 8191]
     assert rel_l2_per_transform(y[rows].cpu().numpy(), _f64(x[rows].cpu().numpy())) <= TOL_F64
-    back = execute_fft_plan(_plan("fft_dit_matrix_batch", n, b, params={"tile": 256},
+    back = execute_fft_plan(_plan("fft_dit_matrix_batch", n, b, params={"tile": tile},
                                   transform_direction="inverse"), y)
     err = (torch.linalg.vector_norm(back - x) / torch.linalg.vector_norm(x)).item()
     assert err <= 2 * TOL_F64
+    assert _lib.device_status(0) == 0
+
+
+@pytest.mark.parametrize("log2n", [13, 14, 15, 16])
+def test_fused_single_pass_batches_and_ring_reuse(log2n):
+    """The fused single pass (tile = N, batch >= 2): ragged batches, and a batch
+    past the scratch ring so slots are reused (the ring holds 3072 tickets of
+    16 KiB: 96 transforms at 2^16 .. 768 at 2^13); forward against float64 on
+    every row, inverse with ortho norm against float64, one launch per call,
+    and no bounded wait expired."""
+    from bfft.entry import native_plan_for
+
+    n = 1 << log2n
+    ring = 3072 * 16384 // (8 * n)
+    rng = np.random.default_rng(100 + log2n)
+    for b in (2, 3, 37, ring + 45):
+        x = cplx(rng, (b, n))
+        t = dev(x)
+        p = _plan("fft_dit_matrix_batch", n, b, params={"tile": n})
+        assert native_plan_for(p, 0).launches == 1
+        got = host(execute_fft_plan(p, t))
+        assert rel_l2_per_transform(got, _f64(x)) <= TOL_F64, (n, b)
+        pi = _plan("fft_dit_matrix_batch", n, b, params={"tile": n}, transform_direction="inverse", norm="ortho")
+        yi = host(execute_fft_plan(pi, t))
+        assert rel_l2_per_transform(yi, np.fft.ifft(x.astype(np.complex128), norm="ortho")) <= TOL_F64, (n, b)
+    assert _lib.device_status(0) == 0
 
 
 @pytest.mark.parametrize("log2n", [13, 14, 15, 16])
