@@ -42,20 +42,25 @@ struct FusedGeo {
     using GA = PassTGeo<LA, 1>;  // phase A: column FFTs of N1, rows out (bulk copies)
     using GB = PassTGeo<LB, 0>;  // phase B: column FFTs of N2 over the slot, columns out (TMA store)
     static constexpr int N1 = 1 << LA, N2 = 1 << LB;
-    static constexpr int CONSUMERS = 256;
+    // consumers carry two columns each (paired FP32x2 arithmetic): half the
+    // threads of the column-tile geometry
+    static constexpr int CONSUMERS = 128;
     static constexpr int THREADS = CONSUMERS + 64;  // + the loader and the storer warps
-    static_assert(GA::THREADS == CONSUMERS && GB::THREADS == CONSUMERS, "256-thread column tiles");
+    static_assert(GA::THREADS == 2 * CONSUMERS && GB::THREADS == 2 * CONSUMERS, "256-lane column tiles");
+    static constexpr int NPA = GA::K / 2, NPB = GB::K / 2;  // column pairs per tile
     static constexpr int SB = GA::SB > GB::SB ? GA::SB : GB::SB;
     static constexpr int STAGES = 3;
     static constexpr int TA = N2 / GA::K;  // phase-A tiles per transform
     static constexpr int TB = N1 / GB::K;  // phase-B tiles per transform
     static_assert(TA >= 1 && TB >= 1, "N1 * N2 >= 4096");
-    static constexpr int TWA = tw_total(LA), TWB = tw_total(LB);
+    // pair twiddle tables (16 bytes an entry), one table when both phases have the same length
+    static constexpr bool SHARED_TW = LA == LB;
+    static constexpr int TWA = tw_total(LA), TWB = SHARED_TW ? 0 : tw_total(LB);
+    static constexpr int COLTW = GA::COLTW ? 16 * NPA : 0;  // column-factor pairs of phase A
     // alignment slack, stages, control block (mbarriers, the stage items), tables; no static
     // shared memory, so the launcher may raise the dynamic limit to the full 227 KiB
     static constexpr int CTRL = 256;
-    static constexpr size_t SMEM =
-        128 + (size_t)STAGES * SB + CTRL + (size_t)(TWA + TWB + GA::COLTW_ENTRIES) * sizeof(float2);
+    static constexpr size_t SMEM = 128 + (size_t)STAGES * SB + CTRL + (size_t)(TWA + TWB + COLTW) * sizeof(CPair);
 };
 
 __device__ __forceinline__ uint64_t policy_evict_first() {
@@ -150,6 +155,7 @@ __global__ void __launch_bounds__(FusedGeo<LA, LB>::THREADS, 2)
     constexpr int ST = G::STAGES;
     constexpr int NC = G::CONSUMERS;
     static_assert(8 * 3 * ST + ST * sizeof(FusedItem) + sizeof(int) <= G::CTRL, "control block");
+    static_assert(G::CONSUMERS % 32 == 0, "whole consumer warps");
     extern __shared__ unsigned char smem_raw[];
     unsigned char* base =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
@@ -159,9 +165,9 @@ __global__ void __launch_bounds__(FusedGeo<LA, LB>::THREADS, 2)
     uint64_t* empty = staged + ST;
     FusedItem* s_item = reinterpret_cast<FusedItem*>(ctrl + 8 * 3 * ST);
     volatile int* s_abort = reinterpret_cast<volatile int*>(ctrl + 8 * 3 * ST + ST * sizeof(FusedItem));
-    float2* twA = reinterpret_cast<float2*>(ctrl + G::CTRL);
-    float2* twB = twA + G::TWA;
-    float2* coltw = twB + G::TWB;
+    CPair* twA = reinterpret_cast<CPair*>(ctrl + G::CTRL);
+    CPair* twB = G::SHARED_TW ? twA : twA + G::TWA;
+    CPair* coltw = twA + G::TWA + G::TWB;
     auto stage = [&](int s) { return reinterpret_cast<float2*>(base + s * G::SB); };
 
     const int tid = threadIdx.x;
@@ -175,15 +181,15 @@ __global__ void __launch_bounds__(FusedGeo<LA, LB>::THREADS, 2)
         fence_proxy_async_smem();
         *s_abort = 0;
     }
-    fill_stockham_twiddles<LA>(twA);
-    fill_stockham_twiddles<LB>(twB);
+    fill_pair_twiddles<LA>(twA);
+    if constexpr (!G::SHARED_TW) fill_pair_twiddles<LB>(twB);
     SmemTwiddle<2> twiddle;  // W_N lookups (phase-A post-twiddle), staged in shared memory when they fit
     {
         PassArgs pa{};
         pa.tw = a.tw;
         pa.tw_smem_entries = a.tw_smem_entries;
         pa.tw_smem_levels = a.tw_smem_levels;
-        twiddle.setup(coltw + GA::COLTW_ENTRIES, pa);
+        twiddle.setup(reinterpret_cast<float2*>(coltw + G::COLTW), pa);
     }
     __syncthreads();  // the last CTA-wide barrier: the warps part ways here
 
@@ -331,8 +337,9 @@ __global__ void __launch_bounds__(FusedGeo<LA, LB>::THREADS, 2)
     }
     if (tid >= NC) return;
 
-    // ==================================================== consumers (256 threads)
-    const float osr = a.scale, osi = a.conj_out ? -a.scale : a.scale;
+    // ==================================================== consumers (128 threads, a column pair each)
+    const u64 zero = 0;
+    const u64 sre = f2splat(a.scale), sim = f2splat(a.conj_out ? -a.scale : a.scale);
     const bool scaled = a.scale != 1.0f || a.conj_out;
     for (int64_t q = 0;; ++q) {
         const int s = (int)(q % ST);
@@ -342,48 +349,59 @@ __global__ void __launch_bounds__(FusedGeo<LA, LB>::THREADS, 2)
         const FusedItem cur = s_item[s];
         if (cur.kind == 0 || *s_abort) break;
         float2* buf = stage(s);
+        const float4* buf4 = reinterpret_cast<const float4*>(buf);
         if (cur.kind == 1) {
             // ---------------- phase A: column FFTs of N1, post-twiddle W_N^{k1 n2}, staged as rows
-            const int cl = tid % GA::K, t = tid / GA::K;
-            const uint32_t n2 = (uint32_t)(cur.idx * GA::K + cl);
-            float2 tb = make_float2(1.f, 0.f);
+            constexpr int NP = G::NPA;
+            const int p = tid % NP, t = tid / NP;  // columns 2p, 2p + 1 of the tile
+            const uint32_t nA = (uint32_t)(cur.idx * GA::K + 2 * p), nB = nA + 1;
+            CPair tb{};
             if constexpr (GA::COLTW) {
 #pragma unroll
                 for (int j = 0; j < GA::CPT; ++j) {
                     const int m = t + j * GA::TF;
-                    if (m < 16) coltw[m * GA::K + cl] = twiddle(static_cast<uint32_t>(m * GA::TF) * n2);
+                    const uint32_t e = static_cast<uint32_t>(m * GA::TF);
+                    if (m < 16) coltw[m * NP + p] = cp_make(twiddle(e * nA), twiddle(e * nB));
                 }
-                tb = twiddle(static_cast<uint32_t>(t) * n2);
+                tb = cp_make(twiddle(static_cast<uint32_t>(t) * nA), twiddle(static_cast<uint32_t>(t) * nB));
             }
-            float2 v[16];
+            CPair v[16];
 #pragma unroll
             for (int m = 0; m < 16; ++m) {
-                float2 val = buf[(t + m * GA::TF) * GA::K + cl];
-                if (a.conj_in) val.y = -val.y;
-                v[m] = val;
+                const float4 x = buf4[(t + m * GA::TF) * NP + p];
+                v[m] = CPair{f2pack(x.x, x.z), f2pack(x.y, x.w)};
+                if (a.conj_in) v[m].im = f2sub(zero, v[m].im);
             }
             group_sync<NC>();  // the tile is now the exchange area; the column factors are published
-            stockham_passes<LA, 0, 16, GA::TF, GA::K, true, NC>(v, t, buf + cl, twA);
+            pair_passes<LA, 0, GA::TF, NP, NC>(v, t, reinterpret_cast<ulonglong2*>(buf) + p, twA);
 #pragma unroll
             for (int m = 0; m < 16; ++m) {
                 const uint32_t k = static_cast<uint32_t>(t + m * GA::TF);
-                float2 w;
-                if constexpr (GA::COLTW) w = cmul(tb, coltw[m * GA::K + cl]);
-                else w = twiddle(k * n2);
-                buf[cl * (GA::L + GA::RPAD) + k] = cmul(v[m], w);
+                CPair w;
+                if constexpr (GA::COLTW) w = cp_mul(tb, coltw[m * NP + p]);
+                else w = cp_make(twiddle(k * nA), twiddle(k * nB));
+                const CPair y = cp_mul(v[m], w);
+                buf[(2 * p) * (GA::L + GA::RPAD) + k] = cp_first(y);
+                buf[(2 * p + 1) * (GA::L + GA::RPAD) + k] = cp_second(y);
             }
         } else {
             // ---------------- phase B: column FFTs of N2 over the slot, epilogue, staged as columns of X
-            const int cl = tid % GB::K, t = tid / GB::K;
-            float2 v[16];
-#pragma unroll
-            for (int m = 0; m < 16; ++m) v[m] = buf[(t + m * GB::TF) * GB::K + cl];
-            group_sync<NC>();
-            stockham_passes<LB, 0, 16, GB::TF, GB::K, true, NC>(v, t, buf + cl, twB);
+            constexpr int NP = G::NPB;
+            const int p = tid % NP, t = tid / NP;
+            CPair v[16];
 #pragma unroll
             for (int m = 0; m < 16; ++m) {
-                const float2 val = v[m];
-                buf[(t + m * GB::TF) * GB::K + cl] = scaled ? make_float2(val.x * osr, val.y * osi) : val;
+                const float4 x = buf4[(t + m * GB::TF) * NP + p];
+                v[m] = CPair{f2pack(x.x, x.z), f2pack(x.y, x.w)};
+            }
+            group_sync<NC>();
+            pair_passes<LB, 0, GB::TF, NP, NC>(v, t, reinterpret_cast<ulonglong2*>(buf) + p, twB);
+            float4* out4 = reinterpret_cast<float4*>(buf);
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+                CPair y = v[m];
+                if (scaled) y = CPair{f2mul(y.re, sre), f2mul(y.im, sim)};
+                out4[(t + m * GB::TF) * NP + p] = make_float4(f2lo(y.re), f2lo(y.im), f2hi(y.re), f2hi(y.im));
             }
         }
         fence_proxy_async_smem();

@@ -959,6 +959,7 @@ static cudaError_t launch_pass_l(int layout, int lmap, int smap, const float2* i
 }  // namespace bfft
 
 #include "bfft_pass_tma.cuh"
+#include "bfft_pair.cuh"
 #include "bfft_fused.cuh"
 
 namespace bfft {
