@@ -55,10 +55,19 @@ WORKLOADS = {
 SEED = 1234
 # One metric string for both arms (BASELINE.json's metric), so the two lines compare.
 METRIC = "complex64 C2C FFT GFLOP/s (5N\u00b7log2N/t) and HBM GB/s vs roofline, 1-8 B200"
-# DRAM bytes per launch of the dominant kernel, from an ncu capture of a small
-# case of the same flow scaled by the elements processed.  Keyed by workload and plan.
+# DRAM bytes (read + write) per launch of the dominant kernel, from ncu
+# captures of the same flow: config 5a from a 512-row case scaled by the rows
+# processed; configs 3 and 4 captured at their full size.  Keyed by workload
+# and transform length.
 PROFILED_TRAFFIC = {
-    ("5a", "fft_dit_matrix_batch", 256): (7.82e9, "ncu dram__bytes_read+write, 512-row case scaled x16"),
+    ("5a", 65536): (10.31e9, "k_fused_fft<8,8>: 291.5 + 353.1 MB at B=512, scaled x16"),
+    ("sweep", 2): (217.6e6, "k_rows_regs<1>"), ("sweep", 16): (215.2e6, "k_rows_shfl<4>"),
+    ("sweep", 64): (217.7e6, "k_rows_shfl<6>"), ("sweep", 128): (215.0e6, "k_rows_shfl128"),
+    ("sweep", 256): (214.3e6, "k_pass_tma_rows<8>"), ("sweep", 1024): (218.0e6, "k_pass_tma_rows<10>"),
+    ("sweep", 4096): (221.4e6, "k_pass_tma_rows<12>"), ("sweep", 8192): (280.2e6, "k_fused_fft<7,6>"),
+    ("sweep", 32768): (289.8e6, "k_fused_fft<8,7>"), ("sweep", 131072): (220.9e6, "k_pass_tma<9,0,0>"),
+    ("sweep", 1048576): (219.5e6, "k_pass_tma<7,0,0>"),
+    ("c4-r2c", 65536): (111.1e6, "k_fused_fft<8,7> (the core)"), ("c4-c2r", 65536): (111.5e6, "k_fused_fft<8,7>"),
 }
 FALLBACK_HBM_GBS = 6650.0
 
@@ -257,14 +266,15 @@ def choose_plan(n: int, b: int, tt: str = "c2c", td: str = "forward"):
                              fallback=False, executed="fft_dit_matrix_batch" if b > 1 else "fft_dit_matrix",
                              block=256, flow_id=real_flow, flow_realization="matrix-resident",
                              processing_unit="dense-dot-fft64",
-                             params={"tile": half if half <= 4096 else 256, "rows": 1, "variant": "spread",
-                                     "batch": b, "real_flow": real_flow},
+                             params={"tile": half if half <= 4096 or (half <= 65536 and b >= 2) else 256,
+                                     "rows": 1, "variant": "spread", "batch": b, "real_flow": real_flow},
                              transform_type=tt, transform_direction=td), "explicit"
-    # one CTA-resident pass up to 4096 points; beyond, a 256-point local group
-    # and tail passes of <= 2^9 points (every pass on the TMA-staged kernels);
-    # past 2^26 a 128-point local group (N = 2^30: 7 + 8 + 8 + 7 stages measured
-    # 1.5-2.5 % faster than 8 + 8 + 7 + 7)
-    tile = n if n <= 4096 else (256 if n <= (1 << 26) else 128)
+    # one CTA-resident pass up to 4096 points; 2^13..2^16 with a batch, the
+    # fused single pass (tile = N); beyond, a 256-point local group and tail
+    # passes of <= 2^9 points (every pass on the TMA-staged kernels); past 2^26
+    # a 128-point local group (N = 2^30: 7 + 8 + 8 + 7 stages measured 1.5-2.5 %
+    # faster than 8 + 8 + 7 + 7)
+    tile = n if n <= 4096 or (n <= 65536 and b >= 2) else (256 if n <= (1 << 26) else 128)
     executed = "fft_dit_matrix_batch" if b > 1 else "fft_dit_matrix"
     return ExecutionPlan(n=n, batch=b, direction="dit", precision="fp32", selection_source="table",
                          reason="explicit B200 local-fused core (selector abstained: " + p.reason + ")",
@@ -494,12 +504,15 @@ def run_batch(args, wl, ctx) -> dict:
     per_launch_ms = ms_step / max(native.launches, 1)
     bytes_per_launch = float((in_row + out_row) * b) if tt != "c2c" else 16.0 * n * b
     achieved = bytes_per_launch / (per_launch_ms / 1e3) / 1e9
-    traffic = PROFILED_TRAFFIC.get((args.workload, plan.executed, int((plan.params or {}).get("tile", 0))))
+    traffic = PROFILED_TRAFFIC.get((args.workload, n))
     # per launch on this rank (b of the workload's rows), like `achieved`
+    traffic_src = traffic[1] if traffic is not None and args.batch is None else None
     traffic = traffic[0] * b / wl["batch"] if traffic is not None and args.batch is None else None
-    roofline = {"bound": "hbm", "kernel": "k_pass_tma / k_pass (CTA-resident Stockham pass)", "achieved": achieved,
+    kernel = ("k_fused_fft (fused single pass)" if native.launches == 1 and n > 4096 and tt == "c2c"
+              else "k_pass_tma / k_pass_tma_rows / k_rows_shfl (CTA-resident Stockham passes)")
+    roofline = {"bound": "hbm", "kernel": kernel, "achieved": achieved,
                 "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
-                "traffic": traffic, "launches_per_step": native.launches,
+                "traffic": traffic, "traffic_source": traffic_src, "launches_per_step": native.launches,
                 "algorithmic_bytes_per_launch": bytes_per_launch,
                 "transform_hbm_gbs": (in_row + out_row) * b / (ms_step / 1e3) / 1e9}
 
