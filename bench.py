@@ -458,7 +458,7 @@ def api_wall(fn, trials: int) -> dict:
     from bfft import runner
 
     r = runner.time_call_detailed(fn, warmup=3, trials=trials, seed=0)
-    return {"api_ms": r["api_ms"], "kernel_ms": r["kernel_ms"],
+    return {"api_ms": r["api_ms"], "kernel_ms": r["kernel_ms"], "raw": r.get("raw"),
             "protocol": "bfft.runner.time_call_detailed: 3 warm-up calls, interleaved trials, "
                         "torch.cuda.synchronize() after each call; api_ms = host wall time of call + sync"}
 
@@ -716,6 +716,8 @@ def main() -> None:
                     help="trials of the reference-style synchronised API wall-time protocol")
     ap.add_argument("--steps-5b", type=int, default=5, help="timed steps of the config-5b secondary line")
     ap.add_argument("--no-5b", action="store_true", help="skip the config-5b secondary measurement (5a only)")
+    ap.add_argument("--rows-out", default=None,
+                    help="write the raw rows (API wall / device time of every trial, the JSON line) to this file")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", choices=("p2p", "nccl"), default=None,
                     help="5b on 2+ GPUs: fused peer-store exchanges (default) or NCCL all-to-alls")
@@ -744,7 +746,10 @@ def main() -> None:
     res = run_4step(args, wl, ctx) if wl.get("kind") == "4step" else run_batch(args, wl, ctx)
     sec = None
     if args.workload == "5a" and args.batch is None and not args.no_5b:
-        sec = secondary_5b(args, ctx)
+        try:
+            sec = secondary_5b(args, ctx)
+        except Exception as e:  # noqa: BLE001 - the headline line is printed regardless; the error is reported
+            sec = {"workload": "config 5b", "error": f"{type(e).__name__}: {e}"[:300]}
 
     cpu = None
     if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline:
@@ -768,6 +773,10 @@ def main() -> None:
             line["secondary_5b"] = sec
         if wl.get("profile_case"):
             line["profile_case"] = True
+        raw = (line.get("api_wall") or {}).pop("raw", None)
+        if args.rows_out:
+            with open(args.rows_out, "w") as f:
+                json.dump({"line": line, "api_wall_trials": raw}, f, indent=1)
         print(json.dumps(line), flush=True)
     ctx.close()
 

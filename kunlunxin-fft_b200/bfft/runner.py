@@ -501,4 +501,5 @@ def time_call_detailed(fn, warmup: int = 10, trials: int = 50, seed: int = 0) ->
                 "p90": xs[min(len(xs) - 1, int(0.9 * len(xs)))], "trials": len(xs)}
 
     return {"api_ms": stats(api), "kernel_ms": stats(kern),
-            "metric_note": "api_ms = synchronized wall time; kernel_ms = CUDA event device time"}
+            "metric_note": "api_ms = synchronized wall time; kernel_ms = CUDA event device time",
+            "raw": {"api_ms": api, "kernel_ms": kern}}
