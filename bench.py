@@ -646,61 +646,89 @@ def secondary_5b(args, ctx) -> dict:
     res = {"workload": "config 5b: one C2C forward of N=2^30 (8 GiB complex64), slab per rank",
            "exchange": None}
 
-    def make(n):
+    def make(n, order="natural"):
         if ctx.world == 1:
             plan, _ = choose_plan(n, 1)
             return (lambda t: bfft.execute_fft_plan(plan, t)), None, f"{plan.executed} tile {plan.params['tile']}"
-        f = bdist.DistributedFFT(n, device=ctx.dev, exchange=args.exchange)
+        f = bdist.DistributedFFT(n, device=ctx.dev, exchange=args.exchange, output_order=order)
         res["exchange"] = f.exchange
-        return f.execute, f, f"DistributedFFT {f.n1}x{f.n2}, {f.exchange} exchanges"
+        return f.execute, f, f"DistributedFFT {f.n1}x{f.n2}, {f.exchange} exchanges, {order} output"
 
-    # parity at N = 2^24
-    nc = 1 << 24
-    g = torch.Generator(device=ctx.dev).manual_seed(SEED + 77 + ctx.rank)
-    xc = torch.complex(torch.randn(nc // ctx.world, device=ctx.dev, generator=g),
-                       torch.randn(nc // ctx.world, device=ctx.dev, generator=g))
-    fn, obj, _ = make(nc)
-    yc = fn(xc)
-    parts = []
-    for t in (xc, yc):
-        flat = torch.view_as_real(t).reshape(-1).contiguous()
+    def parity(order):
+        """rel L2 at N = 2^24 against float64 numpy.fft (rank 0; None elsewhere)."""
+        nc = 1 << 24
+        g = torch.Generator(device=ctx.dev).manual_seed(SEED + 77 + ctx.rank)
+        xc = torch.complex(torch.randn(nc // ctx.world, device=ctx.dev, generator=g),
+                           torch.randn(nc // ctx.world, device=ctx.dev, generator=g))
+        fn, obj, _ = make(nc, order)
+        yc = fn(xc)
+        parts = []
+        for t in (xc, yc):
+            flat = torch.view_as_real(t).reshape(-1).contiguous()
+            if ctx.world > 1:
+                full = torch.empty(flat.numel() * ctx.world, dtype=flat.dtype, device=ctx.dev)
+                ctx.dist.all_gather_into_tensor(full, flat)
+            else:
+                full = flat
+            parts.append(full)
+        rel = None
+        if ctx.rank == 0:
+            xa = parts[0].view(-1, 2).cpu().numpy().astype(np.float64)
+            ya = parts[1].view(-1, 2).cpu().numpy().astype(np.float64)
+            ref = np.fft.fft(xa[:, 0] + 1j * xa[:, 1])
+            if order == "transposed":  # rank blocks of whole columns k1, one after another
+                ref = ref.reshape(obj.n2, obj.n1).T.reshape(-1)
+            got = ya[:, 0] + 1j * ya[:, 1]
+            rel = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+        del xc, yc, parts, fn, obj
+        ctx.barrier()
+        return nc, rel
+
+    def timed(order):
+        n = 1 << 30
+        slab = n // ctx.world
+        g = torch.Generator(device=ctx.dev).manual_seed(SEED + ctx.rank)
+        x = torch.complex(torch.randn(slab, device=ctx.dev, generator=g),
+                          torch.randn(slab, device=ctx.dev, generator=g))
+        fn, obj, path = make(n, order)
+        for _ in range(3):
+            y = fn(x)
+        del y
+        ms, launches, clocks = ctx.timed(lambda: fn(x), args.steps_5b)
+        ms /= args.steps_5b
+        out = {"path": path, "n": n, "ms_per_step": ms, "steps": args.steps_5b, "warmup": 3,
+               "gflops": gflop(n, 1) / (ms / 1e3), "gpu_launches": int(launches),
+               "transform_hbm_gbs_per_gpu": 16.0 * slab / (ms / 1e3) / 1e9, "clocks": clocks}
+        if obj is not None:
+            # one more (untimed) execution with events between the steps: where the time goes
+            trace = []
+            obj.execute(x, trace=trace)
+            torch.cuda.synchronize(ctx.dev)
+            steps = {}
+            for (_, e0), (name, e1) in zip(trace, trace[1:]):
+                steps.setdefault(name, []).append(round(e0.elapsed_time(e1), 3))
+            out["step_ms_rank"] = {"rank": ctx.rank, "steps": steps}
+            ctx.barrier()
         if ctx.world > 1:
-            full = torch.empty(flat.numel() * ctx.world, dtype=flat.dtype, device=ctx.dev)
-            ctx.dist.all_gather_into_tensor(full, flat)
-        else:
-            full = flat
-        parts.append(full)
-    rel = None
-    if ctx.rank == 0:
-        xa = parts[0].view(-1, 2).cpu().numpy().astype(np.float64)
-        ya = parts[1].view(-1, 2).cpu().numpy().astype(np.float64)
-        ref = np.fft.fft(xa[:, 0] + 1j * xa[:, 1])
-        got = ya[:, 0] + 1j * ya[:, 1]
-        rel = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
-    del xc, yc, parts, fn, obj
-    ctx.barrier()
+            wire = (3.0 if order == "natural" else 2.0) * 8.0 * slab * (ctx.world - 1) / ctx.world
+            out["nvlink"] = {"bytes_per_step_per_gpu": wire, "gbs_per_direction": wire / (ms / 1e3) / 1e9,
+                             "peak_gbs_per_direction": 770.0, "peak_source": "measured peer copy on this pool"}
+        del x, fn, obj
+        torch.cuda.synchronize(ctx.dev)
+        ctx.barrier()
+        return out
 
-    n = 1 << 30
-    slab = n // ctx.world
-    g = torch.Generator(device=ctx.dev).manual_seed(SEED + ctx.rank)
-    x = torch.complex(torch.randn(slab, device=ctx.dev, generator=g), torch.randn(slab, device=ctx.dev, generator=g))
-    fn, obj, path = make(n)
-    for _ in range(3):
-        y = fn(x)
-    del y
-    ms, launches, clocks = ctx.timed(lambda: fn(x), args.steps_5b)
-    ms /= args.steps_5b
-    res.update({"path": path, "n": n, "ms_per_step": ms, "steps": args.steps_5b, "warmup": 3,
-                "gflops": gflop(n, 1) / (ms / 1e3), "gpu_launches": int(launches),
-                "transform_hbm_gbs_per_gpu": 16.0 * slab / (ms / 1e3) / 1e9,
-                "parity_n": nc, "rel_l2_vs_float64": rel, "clocks": clocks})
+    nc, rel = parity("natural")
+    res.update(timed("natural"))
+    res.update({"parity_n": nc, "rel_l2_vs_float64": rel})
     if ctx.world > 1:
-        wire = 3.0 * 8.0 * slab * (ctx.world - 1) / ctx.world
-        res["nvlink"] = {"bytes_per_step_per_gpu": wire, "gbs_per_direction": wire / (ms / 1e3) / 1e9,
-                         "peak_gbs_per_direction": 770.0, "peak_source": "measured peer copy on this pool"}
-    del x, fn, obj
-    torch.cuda.synchronize(ctx.dev)
-    ctx.barrier()
+        # the explicit transposed-output mode: two exchanges, rank r keeps
+        # columns k1 in [r N1/P, (r+1) N1/P) of the N1 x N2 output view
+        nc, rel_t = parity("transposed")
+        t = timed("transposed")
+        t.update({"parity_n": nc, "rel_l2_vs_float64": rel_t,
+                  "layout": "rank r holds out[k1'][k2] = X[k2 N1 + r N1/P + k1']"})
+        res["transposed_output"] = t
     return res
 
 

@@ -159,6 +159,18 @@ BFFT_EXPORT bfft_status bfft_twiddle_table(void* w, int64_t n, int64_t count, in
  * 1 DIT radix-4 digit reversal (:41-57), 2 DIF digit reversal (:60-78). */
 BFFT_EXPORT bfft_status bfft_index_map(int32_t kind, int32_t bits, void* out, int32_t device, void* stream);
 
+/* 16-point DFT of every contiguous row of x ((rows, 16) complex64) on the
+ * tensor cores: the dense-dot form of the reference's local_matrix_kernel
+ * (src/xpu/kernels.py:487-532) with the DFT as a real 32 x 32 matrix, as
+ * tcgen05.mma kind::tf32 products with the 3xTF32 split (x = hi + lo in TF32,
+ * D = lo*Bhi + hi*Blo + hi*Bhi accumulated in FP32).  transform_direction
+ * BFFT_INVERSE conjugates input and output; every output is multiplied by
+ * scale.  Pointers 16-byte aligned, in != out, 1 <= rows < 2^31.
+ * Experimental: no plan selects it (the FP32 row kernels are faster and more
+ * accurate at this size). */
+BFFT_EXPORT bfft_status bfft_tc_dft16_rows(const void* in, void* out, int64_t rows, int32_t transform_direction,
+                                           float scale, int32_t device, void* stream);
+
 /* 4-step C2C without any device allocation -- no counterpart in the reference.
  *
  * For callers that cannot allocate device memory while they run: code inside
@@ -211,8 +223,14 @@ BFFT_EXPORT bfft_status bfft_dist_batch_shard(int64_t batch, int32_t nranks, int
  * the send buffer goes to rank s; chunk p of the receive buffer comes from
  * rank p) and phase k+1 reads the receive buffer of the exchange before it.
  * With nranks = 1 the exchanges are identities (phase k+1 reads phase k's
- * output).  Every phase writes N/P complex64 to `out`; phases 1 and 2 need
- * bfft_dist_workspace_size bytes of workspace.  Row FFT tiles 0 = default. */
+ * output).  Every phase writes N/P complex64 to `out`; phases 1, 2 and 4 need
+ * bfft_dist_workspace_size bytes of workspace.  Row FFT tiles 0 = default.
+ * Transposed-output mode: phase 4 takes the place of phase 2, the third
+ * all-to-all and phase 3,
+ *     phase 0 -> all-to-all -> phase 1 -> all-to-all -> phase 4
+ * and leaves rank r with the (n1/P) x n2 block out[k1'][k2] =
+ * X[k2 n1 + r n1/P + k1'] (whole columns of the n1 x n2 output view) instead
+ * of the natural-order slab. */
 typedef struct bfft_dist_plan_s* bfft_dist_plan_t;
 BFFT_EXPORT bfft_status bfft_dist_plan_create(int64_t n1, int64_t n2, int32_t nranks, int32_t rank,
                                               int32_t transform_direction, int32_t norm, int32_t row_tile1,
@@ -232,7 +250,9 @@ BFFT_EXPORT bfft_status bfft_dist_phase(bfft_dist_plan_t plan, int32_t phase, co
  * where a barrier means every rank's previous phase has completed (the host
  * orders it, e.g. a stream-ordered all-reduce of one word).  Phase 0 reads
  * `in` (the rank's slab), phase 3 writes `out` (the rank's output slab);
- * phases 1 and 2 need bfft_dist_workspace_size bytes of workspace.  No
+ * phases 1 and 2 need bfft_dist_workspace_size bytes of workspace.  The
+ * transposed-output order is barrier -> phase 0 -> barrier -> phase 1 ->
+ * barrier -> phase 4, phase 4 writing the block described above to `out`.  No
  * device-side waits, no multicast: plain stores to peer memory. */
 BFFT_EXPORT bfft_status bfft_dist_p2p_prepare(bfft_dist_plan_t plan, void* exchange_base, void* ipc_handle,
                                               size_t* handle_bytes);

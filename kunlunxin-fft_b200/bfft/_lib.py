@@ -29,7 +29,7 @@ VARIANT_IDS = {"spread": 0, "folded": 1}
 EXPORTS = ("bfft_api_version", "bfft_last_error", "bfft_plan_create", "bfft_plan_workspace_size",
            "bfft_plan_launches", "bfft_execute", "bfft_plan_destroy", "bfft_bit_reverse_permute",
            "bfft_r2c_stitch", "bfft_c2r_pre", "bfft_c2r_unpack", "bfft_twiddle_table",
-           "bfft_index_map", "bfft_launch_counter", "bfft_hybrid_c2c_noalloc",
+           "bfft_index_map", "bfft_launch_counter", "bfft_hybrid_c2c_noalloc", "bfft_tc_dft16_rows",
            "bfft_dist_batch_shard", "bfft_dist_plan_create", "bfft_dist_workspace_size",
            "bfft_dist_phase", "bfft_dist_plan_launches", "bfft_dist_plan_destroy", "bfft_device_status",
            "bfft_stream_plan_create", "bfft_stream_plan_info", "bfft_stream_execute", "bfft_stream_plan_destroy",
@@ -85,6 +85,7 @@ def load() -> ctypes.CDLL:
         L.bfft_twiddle_table.argtypes = [vp, i64, i64, i32, vp]
         L.bfft_index_map.argtypes = [i32, i32, vp, i32, vp]
         L.bfft_hybrid_c2c_noalloc.argtypes = [vp, vp, i64, i64, i64, i32, i32, i32, vp]
+        L.bfft_tc_dft16_rows.argtypes = [vp, vp, i64, i32, ctypes.c_float, i32, vp]
         L.bfft_dist_batch_shard.argtypes = [i64, i32, i32, ctypes.POINTER(i64), ctypes.POINTER(i64)]
         L.bfft_dist_plan_create.argtypes = [i64, i64, i32, i32, i32, i32, i32, i32, i32, ctypes.POINTER(vp)]
         L.bfft_dist_workspace_size.argtypes = [vp, ctypes.POINTER(sz)]
@@ -189,8 +190,8 @@ class NativeDistPlan:
         ws = ctypes.c_size_t()
         check(L.bfft_dist_workspace_size(self.handle, ctypes.byref(ws)), "bfft_dist_workspace_size")
         self.workspace_bytes = int(ws.value)
-        self.launches = []
-        for ph in range(4):
+        self.launches = []  # per phase 0..4 (4: the transposed-output phase)
+        for ph in range(5):
             nl = ctypes.c_int()
             check(L.bfft_dist_plan_launches(self.handle, ph, ctypes.byref(nl)), "bfft_dist_plan_launches")
             self.launches.append(int(nl.value))

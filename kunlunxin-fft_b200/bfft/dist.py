@@ -12,7 +12,11 @@ process per GPU (NCCL over NVLink on B200, ``gloo`` for the CPU tests).
   contiguous slabs, computed with the reference's hybrid 4-step
   decomposition (``src/xpu/adapter_hybrid.py:224-270``) whose three
   transposes become all-to-alls (``all_to_all_single``, equal chunks) between
-  the four device phases of ``bfft_dist_phase``.
+  the four device phases of ``bfft_dist_phase``.  With
+  ``output_order="transposed"`` the last exchange and the two local passes
+  around it are skipped: rank r ends with the (N1/P) x N2 block
+  ``out[k1'][k2] = X[k2 N1 + r N1/P + k1']`` (whole columns of the N1 x N2
+  output view) instead of the slab ``X[r N/P : (r+1) N/P]``.
 
 The device phases come from libbfft.so; there is no CPU fallback.  The
 ``phases`` argument of ``DistributedFFT`` exists so the orchestration can be
@@ -68,7 +72,10 @@ class _NativePhases:
         self.plan = _lib.NativeDistPlan(n1, n2, world, rank, transform_direction=transform_direction, norm=norm,
                                         row_tiles=row_tiles, device=device.index or 0)
         self.ws = torch.empty(max(self.plan.workspace_bytes, 16), dtype=torch.uint8, device=device)
-        self.launches = sum(self.plan.launches)
+        self.natural_launches = sum(self.plan.launches[:4])
+        L = self.plan.launches
+        self.transposed_launches = L[0] + L[1] + L[4]
+        self.launches = self.natural_launches
 
     def empty(self, count: int) -> torch.Tensor:
         return torch.empty(count, dtype=torch.complex64, device=self.device)
@@ -95,7 +102,11 @@ class _NativeP2PPhases(_NativePhases):
             self.plan.p2p_attach(bytes(every.cpu().tolist()))
         else:
             self.plan.p2p_attach_pointers([base])
-        self.launches = sum(self.plan.launches) - 2 * (1 if world > 1 else 0) - 1  # no chunk permutes
+        # no chunk permutes (the scatters place every chunk), and phase 3 is a copy
+        L, permutes = self.plan.launches, (1 if world > 1 else 0)
+        self.natural_launches = L[0] + (L[1] - permutes) + (L[2] - permutes)
+        self.transposed_launches = L[0] + (L[1] - permutes) + (L[4] - permutes)
+        self.launches = self.natural_launches
 
     def phase(self, k: int, x, out) -> None:
         stream = torch.cuda.current_stream(self.device).cuda_stream
@@ -110,11 +121,18 @@ class DistributedFFT:
     contiguous, on its device) and receives ``X[r n/P : (r+1) n/P]`` of the
     transform in natural order, with the reference's ``transform_direction``
     and ``norm`` semantics (src/xpu/entry.py:81-102, :619-621).  P must be a
-    power of two dividing both factors of ``n = n1 * n2``."""
+    power of two dividing both factors of ``n = n1 * n2``.
+
+    ``output_order="transposed"`` (two exchanges instead of three): rank r
+    receives the (N1/P) x N2 block ``out[k1'][k2] = X[k2 N1 + r N1/P + k1']``
+    (``output_view`` reshapes it), for callers that consume the spectrum
+    column-wise or transform back with the matching input order."""
 
     def __init__(self, n: int, *, n1: int | None = None, group=None, transform_direction: str = "forward",
                  norm: str = "backward", device=None, row_tiles: tuple[int, int] = (0, 0), phases=None,
-                 exchange: str | None = None):
+                 exchange: str | None = None, output_order: str = "natural"):
+        if output_order not in ("natural", "transposed"):
+            raise ValueError(f"output_order must be 'natural' or 'transposed', got {output_order!r}")
         if transform_direction not in ("forward", "inverse"):
             raise ValueError(f"transform_direction must be 'forward' or 'inverse', got {transform_direction!r}")
         if norm not in ("none", "forward", "backward", "ortho"):
@@ -143,6 +161,7 @@ class DistributedFFT:
             else:
                 phases = _NativePhases(n1, n2, self.world, self.rank, transform_direction, norm, dev, row_tiles)
         self.exchange = "p2p" if getattr(phases, "p2p", False) else "nccl"
+        self.output_order = output_order
         self.phases = phases
         self._bufs = None
         self._flag = None
@@ -150,7 +169,16 @@ class DistributedFFT:
     @property
     def launches(self) -> int:
         """Device kernels one execute() enqueues on this rank."""
-        return getattr(self.phases, "launches", 0)
+        key = "transposed_launches" if self.output_order == "transposed" else "natural_launches"
+        return getattr(self.phases, key, getattr(self.phases, "launches", 0))
+
+    def output_view(self, out: torch.Tensor) -> torch.Tensor:
+        """``out`` as the rank's 2-D output block: (N2/P, N1) rows of
+        ``X[k2 N1 + k1]`` (natural) or (N1/P, N2) with element [k1'][k2] =
+        ``X[k2 N1 + r N1/P + k1']`` (transposed)."""
+        if self.output_order == "transposed":
+            return out.view(self.n1 // self.world, self.n2)
+        return out.view(self.n2 // self.world, self.n1)
 
     def _buffers(self):
         if self._bufs is None:
@@ -172,7 +200,10 @@ class DistributedFFT:
         dist.all_to_all_single(recv, send, group=self.group)
         return recv
 
-    def execute(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    def execute(self, x: torch.Tensor, out: torch.Tensor | None = None, trace: list | None = None) -> torch.Tensor:
+        """Enqueue one transform on the current stream.  ``trace`` (optional
+        list) receives ``(step, cuda.Event)`` pairs recorded after every phase
+        and exchange, for per-step device times."""
         if not isinstance(x, torch.Tensor):
             raise TypeError("x must be a torch.Tensor")
         if x.dtype != torch.complex64:
@@ -181,26 +212,39 @@ class DistributedFFT:
             raise ValueError(f"x must be a contiguous 1-D slab of {self.slab} points, got {tuple(x.shape)}")
         if out is None:
             out = self.phases.empty(self.slab)
+        mids = (1, 2) if self.output_order == "natural" else (1,)
+        last = 3 if self.output_order == "natural" else 4
+
+        def mark(step):
+            if trace is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                trace.append((step, ev))
+
+        mark("start")
         if self.exchange == "p2p":
             # every phase writes into the other ranks' buffers: all ranks must
             # have finished the previous phase (and the previous execution)
-            self._barrier()
-            self.phases.phase(0, x, None)
-            for k in (1, 2):
+            for k in (0, *mids, last):
                 self._barrier()
-                self.phases.phase(k, None, None)
-            self._barrier()
-            self.phases.phase(3, None, out)
+                mark("barrier")
+                self.phases.phase(k, x if k == 0 else None, out if k == last else None)
+                mark(f"phase{k}")
             return out
         a, b = self._buffers()
         self.phases.phase(0, x, a)
+        mark("phase0")
         cur = self._exchange(a, b)
-        for k in (1, 2):
+        mark("exchange")
+        for k in mids:
             dst = a if cur is b else b
             self.phases.phase(k, cur, dst)
+            mark(f"phase{k}")
             other = b if dst is a else a
             cur = self._exchange(dst, other)
-        self.phases.phase(3, cur, out)
+            mark("exchange")
+        self.phases.phase(last, cur, out)
+        mark(f"phase{last}")
         return out
 
     __call__ = execute

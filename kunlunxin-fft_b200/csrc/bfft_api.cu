@@ -936,6 +936,22 @@ bfft_status bfft_device_status(int32_t device, uint32_t* status, int32_t clear) 
     return BFFT_OK;
 }
 
+bfft_status bfft_tc_dft16_rows(const void* in, void* out, int64_t rows, int32_t transform_direction, float scale,
+                               int32_t device, void* stream) {
+    if (!in || !out) return fail(BFFT_ERR_VALUE, "null pointer");
+    if (in == out) return fail(BFFT_ERR_VALUE, "input and output must not alias");
+    if (((uintptr_t)in | (uintptr_t)out) & 15u) return fail(BFFT_ERR_VALUE, "pointers must be 16-byte aligned");
+    if (rows < 1 || rows > 0x7fffffffLL) return fail(BFFT_ERR_SHAPE, "rows must be in [1, 2^31), got %lld", (long long)rows);
+    if (transform_direction != BFFT_FORWARD && transform_direction != BFFT_INVERSE)
+        return fail(BFFT_ERR_VALUE, "bad transform_direction %d", transform_direction);
+    DeviceGuard g(device);
+    if (!g.ok) return fail(BFFT_ERR_CUDA, "cannot select device %d", device);
+    const int inv = transform_direction == BFFT_INVERSE;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    cudaError_t e = launch_tc_dft16_rows((const float2*)in, (float2*)out, rows, scale, inv, inv, (cudaStream_t)stream);
+    return e == cudaSuccess ? BFFT_OK : cuda_fail(e, "tc_dft16_rows");
+}
+
 bfft_status bfft_twiddle_table(void* w, int64_t n, int64_t count, int32_t device, void* stream) {
     if (!w) return fail(BFFT_ERR_VALUE, "null pointer");
     if (!is_pow2(n)) return fail(BFFT_ERR_SHAPE, "size must be a positive power of two, got %lld", (long long)n);

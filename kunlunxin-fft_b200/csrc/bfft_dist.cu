@@ -20,6 +20,12 @@
 //   phase 3: chunk permute -> out[k2'][k1] (conj and norm scale), which is
 //            X[k2 N1 + k1] for the rank's output slab k2 in [r M2, (r+1) M2)
 //
+// Transposed-output mode replaces phase 2, all-to-all 3 and phase 3 by
+//   phase 4: chunk permute -> [k1'][n2]; length-N2 row FFTs -> out[k1'][k2]
+//            (conj and norm scale), i.e. X[k2 N1 + k1] for k1 = r M1 + k1'
+// so the rank ends holding M1 whole columns k1 of the N1 x N2 output view
+// instead of a contiguous slab: one exchange and two local passes fewer.
+//
 // The exchanges themselves are NCCL all-to-alls issued by the host layer
 // between these calls (bfft/dist.py); every phase only touches this rank's
 // device memory.
@@ -98,43 +104,57 @@ __global__ void __launch_bounds__(256) k_chunk_permute(const V* __restrict__ in,
 // (peers[d], mapped into this process), optionally times W_N^{(row0 + r) c},
 // conjugated and scaled.  A 64 x 32 tile is read row-wise (256-byte runs),
 // held transposed in shared memory, and written as 16-byte stores, 512-byte
-// runs of consecutive r per warp, over NVLink (remote ranks) or locally;
-// every thread fences at system scope after its stores so the host-ordered
-// barrier that follows publishes them.
+// runs of consecutive r per warp, over NVLink (remote ranks) or locally.
+// Persistent: a CTA walks tiles with a grid stride, the next tile's loads
+// issued before this tile's stores, and every thread fences at system scope
+// once, after its last store, so the host-ordered barrier that follows
+// publishes them (a fence per tile halved the kernel's rate).
 constexpr int kSR = 64, kSC = 32;  // scatter tile: rows x cols
 __global__ void __launch_bounds__(256) k_scatter_transpose(const float2* __restrict__ in, float2* const* peers,
                                                            int64_t rows, int64_t cols, int64_t tiles_c,
-                                                           int log2_dc, int64_t dst_ld, int64_t dst_off, TwoLevel tw,
-                                                           int use_tw, uint32_t row0, int conj, float scale) {
+                                                           int64_t ntiles, int log2_dc, int64_t dst_ld,
+                                                           int64_t dst_off, TwoLevel tw, int use_tw, uint32_t row0,
+                                                           int conj, float scale) {
     __shared__ __align__(16) float2 t[kSC][kSR + 2];  // [col][row], rows 16-byte aligned
-    const int64_t tile = blockIdx.x;
-    const int64_t r0 = (tile / tiles_c) * kSR, c0 = (tile % tiles_c) * kSC;
     const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
     const int64_t dmask = ((int64_t)1 << log2_dc) - 1;
+    float2 v[kSR / 8];
+    auto load = [&](int64_t tile) {
+        const int64_t r0 = (tile / tiles_c) * kSR, c0 = (tile % tiles_c) * kSC;
 #pragma unroll
-    for (int j = 0; j < kSR / 8; ++j) {
-        const int rl = ty + 8 * j;
-        const int64_t r = r0 + rl, c = c0 + tx;
-        if (r < rows && c < cols) {
-            float2 v = in[r * cols + c];
-            if (conj) v.y = -v.y;
-            if (use_tw) v = cmul(v, tw_two_level(tw, (row0 + (uint32_t)r) * (uint32_t)c));
-            t[tx][rl] = make_float2(v.x * scale, v.y * scale);
+        for (int j = 0; j < kSR / 8; ++j) {
+            const int64_t r = r0 + ty + 8 * j, c = c0 + tx;
+            v[j] = (r < rows && c < cols) ? in[r * cols + c] : make_float2(0.f, 0.f);
         }
-    }
-    __syncthreads();
+    };
+    int64_t tile = blockIdx.x;
+    if (tile < ntiles) load(tile);
+    for (; tile < ntiles; tile += gridDim.x) {
+        const int64_t r0 = (tile / tiles_c) * kSR, c0 = (tile % tiles_c) * kSC;
 #pragma unroll
-    for (int j = 0; j < kSC / 8; ++j) {
-        const int cl = ty + 8 * j;
-        const int64_t c = c0 + cl, r = r0 + 2 * tx;
-        if (c >= cols || r >= rows) continue;
-        float2* dst = peers[c >> log2_dc] + (c & dmask) * dst_ld + dst_off + r;
-        if (r + 1 < rows && !(reinterpret_cast<uintptr_t>(dst) & 15)) {
-            *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(&t[cl][2 * tx]);
-        } else {
-            dst[0] = t[cl][2 * tx];
-            if (r + 1 < rows) dst[1] = t[cl][2 * tx + 1];
+        for (int j = 0; j < kSR / 8; ++j) {
+            const int rl = ty + 8 * j;
+            float2 w = v[j];
+            if (conj) w.y = -w.y;
+            if (use_tw) w = cmul(w, tw_two_level(tw, (row0 + (uint32_t)(r0 + rl)) * (uint32_t)(c0 + tx)));
+            t[tx][rl] = make_float2(w.x * scale, w.y * scale);
         }
+        __syncthreads();
+        if (tile + gridDim.x < ntiles) load(tile + gridDim.x);  // in flight during the stores
+#pragma unroll
+        for (int j = 0; j < kSC / 8; ++j) {
+            const int cl = ty + 8 * j;
+            const int64_t c = c0 + cl, r = r0 + 2 * tx;
+            if (c >= cols || r >= rows) continue;
+            float2* dst = peers[c >> log2_dc] + (c & dmask) * dst_ld + dst_off + r;
+            if (r + 1 < rows && !(reinterpret_cast<uintptr_t>(dst) & 15)) {
+                *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(&t[cl][2 * tx]);
+            } else {
+                dst[0] = t[cl][2 * tx];
+                if (r + 1 < rows) dst[1] = t[cl][2 * tx + 1];
+            }
+        }
+        __syncthreads();  // the tile buffer is rewritten by the next iteration
     }
     __threadfence_system();
 }
@@ -157,9 +177,16 @@ int ilog2(int64_t v) {
 cudaError_t launch_scatter(const float2* in, float2* const* peers, int64_t rows, int64_t cols, int64_t dc,
                            int64_t dst_ld, int64_t dst_off, const TwoLevel& tw, int use_tw, uint32_t row0, int conj,
                            float scale, cudaStream_t s) {
-    const int64_t tr = (rows + kSR - 1) / kSR, tc = (cols + kSC - 1) / kSC;
-    k_scatter_transpose<<<(unsigned)(tr * tc), dim3(32, 8), 0, s>>>(in, peers, rows, cols, tc, ilog2(dc), dst_ld,
-                                                                    dst_off, tw, use_tw, row0, conj, scale);
+    const int64_t tr = (rows + kSR - 1) / kSR, tc = (cols + kSC - 1) / kSC, ntiles = tr * tc;
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = device_sm_count(dev, &sms);
+    if (e != cudaSuccess) return e;
+    // 8 CTAs of 256 threads fill an SM (warp limit); a few tiles per CTA
+    int64_t grid = (int64_t)sms * 8;
+    if (grid > ntiles) grid = ntiles;
+    k_scatter_transpose<<<(unsigned)grid, dim3(32, 8), 0, s>>>(in, peers, rows, cols, tc, ntiles, ilog2(dc), dst_ld,
+                                                               dst_off, tw, use_tw, row0, conj, scale);
     count_launches(1);
     return cudaGetLastError();
 }
@@ -253,11 +280,12 @@ bfft_status make_row_plan(int64_t n, int64_t batch, int32_t tile, int32_t device
     if (tile > 0) {
         d.tile = tile;
     } else {
-        // Whole rows on chip up to 2^12 points (one CTA), else a 256-point
-        // local group and tail passes of <= 2^9 points, every pass on the
-        // TMA-staged kernels (faster than the cluster kernel on batches).
+        // Whole rows on chip up to 2^12 points (one CTA); 2^13..2^16 with a
+        // batch: tile = N, the fused single-pass kernel (one HBM round trip);
+        // else a 256-point local group and tail passes of <= 2^9 points,
+        // every pass on the TMA-staged kernels.
         const int l = ilog2(n);
-        d.tile = l <= kMaxPassLog2 ? (int32_t)n : 256;
+        d.tile = (l <= kMaxPassLog2 || (l <= 16 && batch >= 2)) ? (int32_t)n : 256;
     }
     d.rows = 1;
     d.glog = 4;
@@ -267,6 +295,10 @@ bfft_status make_row_plan(int64_t n, int64_t batch, int32_t tile, int32_t device
     d.device = device;
     return bfft_plan_create(&d, out);
 }
+
+// The transposed-output phase ends with the row FFTs; conjugation (inverse)
+// and a norm scale other than 1 take one more elementwise pass.
+bool dist_epilogue(const bfft_dist_plan_s* p) { return p->tdir == BFFT_INVERSE || p->scale != 1.0f; }
 
 }  // namespace
 
@@ -363,14 +395,14 @@ bfft_status bfft_dist_workspace_size(bfft_dist_plan_t plan, size_t* bytes) {
 bfft_status bfft_dist_phase(bfft_dist_plan_t plan, int32_t phase, const void* in, void* out, void* workspace,
                             size_t workspace_bytes, void* stream) {
     if (!plan) return dfail(BFFT_ERR_VALUE, "NULL plan");
-    if (phase < 0 || phase > 3) return dfail(BFFT_ERR_VALUE, "phase must be 0..3, got %d", phase);
+    if (phase < 0 || phase > 4) return dfail(BFFT_ERR_VALUE, "phase must be 0..4, got %d", phase);
     if (!in || !out) return dfail(BFFT_ERR_VALUE, "NULL data pointer");
     if (in == out) return dfail(BFFT_ERR_VALUE, "in and out must not alias");
     if (((uintptr_t)in | (uintptr_t)out | (uintptr_t)workspace) & 15)
         return dfail(BFFT_ERR_VALUE, "buffers must be 16-byte aligned");
     size_t need = 0;
     bfft_dist_workspace_size(plan, &need);
-    if ((phase == 1 || phase == 2) && (!workspace || workspace_bytes < need))
+    if ((phase == 1 || phase == 2 || phase == 4) && (!workspace || workspace_bytes < need))
         return dfail(BFFT_ERR_WORKSPACE, "phase %d needs %zu workspace bytes, got %zu", phase, need,
                      workspace ? workspace_bytes : (size_t)0);
     DevGuard g(plan->device);
@@ -415,6 +447,17 @@ bfft_status bfft_dist_phase(bfft_dist_plan_t plan, int32_t phase, const void* in
         case 3:  // recv[s][k2'][k1'] -> out[k2'][s][k1'], conj / norm epilogue
             e = launch_chunk_permute(x, y, P, m2, m1, inv, plan->scale, s);
             break;
+        case 4: {  // transposed output: recv[s][k1'][n2'] -> [k1'][n2] -> out[k1'][k2], conj / norm
+            const float2* rows = x;
+            if (P > 1) {
+                e = launch_chunk_permute(x, a, P, m1, m2, 0, 1.0f, s);
+                rows = a;
+            }
+            if (e == cudaSuccess) st = bfft_execute(plan->row2, rows, y, row_ws, row_ws_bytes, stream);
+            if (st == BFFT_OK && e == cudaSuccess && dist_epilogue(plan))
+                e = launch_scale(y, y, m1 * n2, plan->scale, inv, s);
+            break;
+        }
     }
     if (st != BFFT_OK) return st;
     if (e != cudaSuccess) return dcuda(e, "distributed phase launch");
@@ -423,13 +466,15 @@ bfft_status bfft_dist_phase(bfft_dist_plan_t plan, int32_t phase, const void* in
 
 bfft_status bfft_dist_plan_launches(bfft_dist_plan_t plan, int32_t phase, int* launches) {
     if (!plan || !launches) return dfail(BFFT_ERR_VALUE, "NULL plan or output pointer");
-    if (phase < 0 || phase > 3) return dfail(BFFT_ERR_VALUE, "phase must be 0..3, got %d", phase);
+    if (phase < 0 || phase > 4) return dfail(BFFT_ERR_VALUE, "phase must be 0..4, got %d", phase);
     int k = 0;
-    if (phase == 0 || phase == 3) k = 1;
-    else {
+    if (phase == 0 || phase == 3) {
+        k = 1;
+    } else {
         int r = 0;
         bfft_plan_launches(phase == 1 ? plan->row1 : plan->row2, &r);
-        k = r + 1 + (plan->nranks > 1 ? 1 : 0);
+        if (phase == 4) k = r + (plan->nranks > 1 ? 1 : 0) + (dist_epilogue(plan) ? 1 : 0);
+        else k = r + 1 + (plan->nranks > 1 ? 1 : 0);
     }
     *launches = k;
     return BFFT_OK;
@@ -524,13 +569,14 @@ bfft_status bfft_dist_p2p_phase(bfft_dist_plan_t plan, int32_t phase, const void
                                 size_t workspace_bytes, void* stream) {
     if (!plan) return dfail(BFFT_ERR_VALUE, "NULL plan");
     if (!plan->attached) return dfail(BFFT_ERR_VALUE, "peer-to-peer phases need bfft_dist_p2p_attach first");
-    if (phase < 0 || phase > 3) return dfail(BFFT_ERR_VALUE, "phase must be 0..3, got %d", phase);
-    if ((phase == 0 && !in) || (phase == 3 && !out)) return dfail(BFFT_ERR_VALUE, "NULL data pointer");
+    if (phase < 0 || phase > 4) return dfail(BFFT_ERR_VALUE, "phase must be 0..4, got %d", phase);
+    if ((phase == 0 && !in) || ((phase == 3 || phase == 4) && !out))
+        return dfail(BFFT_ERR_VALUE, "NULL data pointer");
     if (((uintptr_t)in | (uintptr_t)out | (uintptr_t)workspace) & 15)
         return dfail(BFFT_ERR_VALUE, "buffers must be 16-byte aligned");
     size_t need = 0;
     bfft_dist_workspace_size(plan, &need);
-    if ((phase == 1 || phase == 2) && (!workspace || workspace_bytes < need))
+    if ((phase == 1 || phase == 2 || phase == 4) && (!workspace || workspace_bytes < need))
         return dfail(BFFT_ERR_WORKSPACE, "phase %d needs %zu workspace bytes, got %zu", phase, need,
                      workspace ? workspace_bytes : (size_t)0);
     DevGuard g(plan->device);
@@ -563,6 +609,11 @@ bfft_status bfft_dist_p2p_phase(bfft_dist_plan_t plan, int32_t phase, const void
             break;
         case 3:  // X1 holds X[k2 N1 + k1] for k2 in this rank's slab
             e = cudaMemcpyAsync(out, x1, sizeof(float2) * slab, cudaMemcpyDeviceToDevice, s);
+            break;
+        case 4:  // transposed output: rows of X2 -> out[k1'][k2], conj / norm
+            st = bfft_execute(plan->row2, x2, out, row_ws, row_ws_bytes, stream);
+            if (st == BFFT_OK && dist_epilogue(plan))
+                e = launch_scale((float2*)out, (float2*)out, m1 * n2, plan->scale, inv, s);
             break;
     }
     if (st != BFFT_OK) return st;

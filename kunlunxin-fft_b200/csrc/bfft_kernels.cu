@@ -434,8 +434,8 @@ __global__ void k_c2r_unpack(const float2* __restrict__ u, float2* __restrict__ 
     }
 }
 
-__global__ void k_scale(const float2* __restrict__ x, float2* __restrict__ y, int64_t count,
-                        float scale, int conj) {
+// Elementwise conj / scale; x == y (in place) is allowed.
+__global__ void k_scale(const float2* x, float2* y, int64_t count, float scale, int conj) {
     for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < count;
          g += (int64_t)gridDim.x * blockDim.x)
         y[g] = out_c(x[g], conj, scale);
@@ -961,6 +961,7 @@ static cudaError_t launch_pass_l(int layout, int lmap, int smap, const float2* i
 #include "bfft_pass_tma.cuh"
 #include "bfft_pair.cuh"
 #include "bfft_fused.cuh"
+#include "bfft_tc.cuh"
 
 namespace bfft {
 

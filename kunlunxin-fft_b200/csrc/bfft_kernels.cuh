@@ -92,6 +92,10 @@ cudaError_t launch_fused_fft(int log2n, const float2* in, float2* out, void* wor
 cudaError_t read_device_status(unsigned* status, bool clear);
 
 // SM count of `dev`, cached after the first query (thread-safe).
+// 16-point DFT of each contiguous row of `rows` x 16 complex64 on the tensor
+// cores (3xTF32 tcgen05.mma); conj_in / conj_out give the inverse.
+cudaError_t launch_tc_dft16_rows(const float2* in, float2* out, int64_t rows, float scale, int conj_in, int conj_out,
+                                 cudaStream_t s);
 cudaError_t device_sm_count(int dev, int* sms);
 
 // Library-wide error message (bfft_last_error) and launch counter.

@@ -75,24 +75,39 @@ class NumpyPhases:
             if self.inv:
                 out = np.conj(out)
             return (out * self.scale).astype(self.dtype)
-        raise ValueError(f"phase must be 0..3, got {k}")
+        if k == 4:  # transposed output: recv[s][k1'][n2'] -> [k1'][n2] -> FFT -> [k1'][k2]
+            rows = x.reshape(p, m1, m2).transpose(1, 0, 2).reshape(m1, n2)
+            h = self._fft_rows(rows).reshape(-1)
+            if self.inv:
+                h = np.conj(h)
+            return (h * self.scale).astype(self.dtype)
+        raise ValueError(f"phase must be 0..4, got {k}")
+
+
+def transposed_slab(X: np.ndarray, n1: int, n2: int, nranks: int, rank: int) -> np.ndarray:
+    """What rank ``rank`` holds after the transposed-output flow, given the
+    whole transform X in natural order: the (N1/P) x N2 block
+    out[k1'][k2] = X[k2 N1 + rank N1/P + k1']."""
+    m1 = n1 // nranks
+    return np.ascontiguousarray(X.reshape(n2, n1).T[rank * m1:(rank + 1) * m1, :]).reshape(-1)
 
 
 def emulate(x: np.ndarray, n1: int, n2: int, nranks: int, transform_direction: str = "forward",
-            norm: str = "backward", phase_fns=None) -> np.ndarray:
+            norm: str = "backward", phase_fns=None, output_order: str = "natural") -> np.ndarray:
     """Run all ranks' phases in one process with the all-to-alls done by
-    array slicing; returns the concatenated output slabs (= the whole
-    transform in natural order).  ``phase_fns[r](k, x)`` defaults to
-    ``NumpyPhases``."""
+    array slicing; returns the concatenated output slabs (natural order: the
+    whole transform; transposed: the ranks' ``transposed_slab`` blocks one
+    after another).  ``phase_fns[r](k, x)`` defaults to ``NumpyPhases``."""
     n = n1 * n2
     slab = n // nranks
     chunk = slab // nranks
     if phase_fns is None:
         phase_fns = [NumpyPhases(n1, n2, nranks, r, transform_direction, norm).phase for r in range(nranks)]
     bufs = [x[r * slab:(r + 1) * slab] for r in range(nranks)]
-    for k in range(4):
+    seq = (0, 1, 2, 3) if output_order == "natural" else (0, 1, 4)
+    for k in seq:
         outs = [phase_fns[r](k, bufs[r]) for r in range(nranks)]
-        if k == 3:
+        if k in (3, 4):
             return np.concatenate([np.asarray(o) for o in outs])
         bufs = [np.concatenate([np.asarray(outs[s])[r * chunk:(r + 1) * chunk] for s in range(nranks)])
                 for r in range(nranks)]

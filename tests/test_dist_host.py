@@ -97,28 +97,37 @@ def _rank_main(rank, world, port, cases, results):
     import datetime
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        for idx, (n1, n2, tdir, norm, seed) in enumerate(cases):
+        for idx, (n1, n2, tdir, norm, seed, *order) in enumerate(cases):
+            order = order[0] if order else "natural"
             n = n1 * n2
             rng = np.random.default_rng(seed)
             x = (rng.standard_normal(n) + 1j * rng.standard_normal(n)).astype(np.complex64)
             slab = n // world
             f = bdist.DistributedFFT(n, n1=n1, transform_direction=tdir, norm=norm,
-                                     phases=HostPhases(n1, n2, world, rank, tdir, norm))
+                                     phases=HostPhases(n1, n2, world, rank, tdir, norm), output_order=order)
             assert (f.world, f.rank) == (world, rank)
-            y = f.execute(torch.from_numpy(x[rank * slab:(rank + 1) * slab].copy())).numpy()
+            y = f.execute(torch.from_numpy(x[rank * slab:(rank + 1) * slab].copy()))
+            assert f.output_view(y).shape == ((n1 // world, n2) if order == "transposed" else (n2 // world, n1))
+            y = y.numpy()
             xd = x.astype(np.complex128)
             ref = np.fft.fft(xd, norm=norm if norm != "none" else "backward") if tdir == "forward" else \
                 np.fft.ifft(xd, norm=norm if norm != "none" else "forward")
             if norm == "none" and tdir == "forward":
                 ref = np.fft.fft(xd)
-            ref = ref[rank * slab:(rank + 1) * slab]
+            if order == "transposed":
+                ref = dist_oracle.transposed_slab(ref, n1, n2, world, rank)
+            else:
+                ref = ref[rank * slab:(rank + 1) * slab]
             results[(rank, idx)] = float(np.linalg.norm(y - ref) / np.linalg.norm(ref))
     finally:
         dist.destroy_process_group()
 
 
 CASES = [(32, 32, "forward", "backward", 1), (64, 16, "forward", "ortho", 2), (16, 64, "inverse", "backward", 3),
-         (32, 32, "inverse", "forward", 4), (8, 128, "forward", "none", 5)]
+         (32, 32, "inverse", "forward", 4), (8, 128, "forward", "none", 5),
+         # transposed-output mode: two exchanges, each rank ends with whole columns k1
+         (32, 32, "forward", "backward", 6, "transposed"), (16, 64, "inverse", "ortho", 7, "transposed"),
+         (64, 16, "inverse", "none", 8, "transposed")]
 
 
 @pytest.mark.parametrize("world", [2, 4])
@@ -143,3 +152,17 @@ def test_emulated_ranks_match_numpy():
         x = rng.standard_normal(n) + 1j * rng.standard_normal(n)
         y = dist_oracle.emulate(x, n1, n2, p)
         assert np.linalg.norm(y - np.fft.fft(x)) / np.linalg.norm(y) < 1e-12
+        yt = dist_oracle.emulate(x, n1, n2, p, output_order="transposed")
+        ref = np.concatenate([dist_oracle.transposed_slab(np.fft.fft(x), n1, n2, p, r) for r in range(p)])
+        assert np.linalg.norm(yt - ref) / np.linalg.norm(ref) < 1e-12
+
+
+def test_output_order_validation():
+    ph = HostPhases(16, 16, 1, 0)
+    with pytest.raises(ValueError):
+        bdist.DistributedFFT(256, n1=16, phases=ph, output_order="bitreversed")
+    f = bdist.DistributedFFT(256, n1=16, phases=ph, output_order="transposed")
+    x = (np.arange(256) * (1 + 0.5j)).astype(np.complex64)
+    y = f.execute(torch.from_numpy(x)).numpy()
+    ref = np.fft.fft(x.astype(np.complex128)).reshape(16, 16).T.reshape(-1)
+    assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < 1e-6

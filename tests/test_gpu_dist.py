@@ -46,7 +46,8 @@ def _native_phase_fns(n1, n2, p, tdir="forward", norm="backward", row_tiles=(0, 
     return [make(r) for r in range(p)], plans
 
 
-def _emulate_device(x, n1, n2, p, tdir="forward", norm="backward", row_tiles=(0, 0), check_phases=True):
+def _emulate_device(x, n1, n2, p, tdir="forward", norm="backward", row_tiles=(0, 0), check_phases=True,
+                    output_order="natural"):
     """All ranks' native phases with the exchanges done by device slicing;
     each phase is also compared with the host restatement on the same input."""
     fns, _ = _native_phase_fns(n1, n2, p, tdir, norm, row_tiles)
@@ -54,7 +55,7 @@ def _emulate_device(x, n1, n2, p, tdir="forward", norm="backward", row_tiles=(0,
     n = n1 * n2
     slab, chunk = n // p, n // (p * p)
     bufs = [torch.from_numpy(x[r * slab:(r + 1) * slab].copy()).to(DEV) for r in range(p)]
-    for k in range(4):
+    for k in ((0, 1, 2, 3) if output_order == "natural" else (0, 1, 4)):
         outs = [fns[r](k, bufs[r]) for r in range(p)]
         if check_phases:
             for r in range(p):
@@ -62,7 +63,7 @@ def _emulate_device(x, n1, n2, p, tdir="forward", norm="backward", row_tiles=(0,
                 got = outs[r].cpu().numpy()
                 err = np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30)
                 assert err < 1e-6, (n1, n2, p, r, k, err)
-        if k == 3:
+        if k in (3, 4):
             return np.concatenate([o.cpu().numpy() for o in outs])
         bufs = [torch.cat([outs[s][r * chunk:(r + 1) * chunk] for s in range(p)]) for r in range(p)]
 
@@ -90,6 +91,33 @@ def test_native_phases_directions_and_norms(tdir, norm):
     assert rel_l2_per_transform(y, ref) <= TOL_F64
 
 
+def _ref_transform(x, tdir, norm):
+    xd = x.astype(np.complex128)
+    if tdir == "forward":
+        return np.fft.fft(xd, norm=norm if norm != "none" else "backward")
+    return np.fft.ifft(xd, norm=norm if norm != "none" else "forward")
+
+
+def _transposed_ref(X, n1, n2, p):
+    return np.concatenate([dist_oracle.transposed_slab(X, n1, n2, p, r) for r in range(p)])
+
+
+@pytest.mark.parametrize("n1, n2, p, tdir, norm", [(1024, 1024, 2, "forward", "backward"),
+                                                   (256, 4096, 4, "inverse", "backward"),
+                                                   (4096, 256, 8, "forward", "ortho"),
+                                                   (512, 512, 1, "inverse", "none"),
+                                                   (1 << 14, 1 << 13, 4, "forward", "backward")])
+def test_native_phases_transposed_output(n1, n2, p, tdir, norm):
+    """Transposed-output mode (phase 4 after the second exchange): each phase
+    against the host restatement, and every rank's (N1/P) x N2 block against
+    the matching columns of float64 numpy.fft."""
+    rng = np.random.default_rng(n1 + 5 * n2 + p)
+    x = cplx(rng, n1 * n2)
+    y = _emulate_device(x, n1, n2, p, tdir, norm, output_order="transposed", check_phases=n1 * n2 <= 1 << 22)
+    ref = _transposed_ref(_ref_transform(x, tdir, norm), n1, n2, p)
+    assert rel_l2_per_transform(y, ref) <= TOL_F64
+
+
 def test_distributed_fft_single_rank_and_row_tiles():
     """DistributedFFT without a process group (P = 1), default and explicit
     row-FFT tiles, and the phase launch counts it reports."""
@@ -106,10 +134,12 @@ def test_distributed_fft_single_rank_and_row_tiles():
         assert rel_l2_per_transform(y.cpu().numpy(), ref) <= TOL_F64, tiles
 
 
+@pytest.mark.parametrize("output_order", ["natural", "transposed"])
 @pytest.mark.parametrize("n1, n2, p, tdir, norm", [(1024, 1024, 2, "forward", "backward"),
                                                    (256, 4096, 4, "inverse", "backward"),
-                                                   (4096, 512, 8, "forward", "ortho"), (512, 512, 1, "forward", "none")])
-def test_p2p_phases_emulated_ranks(n1, n2, p, tdir, norm):
+                                                   (4096, 512, 8, "forward", "ortho"), (512, 512, 1, "forward", "none"),
+                                                   (1 << 13, 1 << 13, 2, "forward", "backward")])
+def test_p2p_phases_emulated_ranks(n1, n2, p, tdir, norm, output_order):
     """Peer-to-peer mode: the exchanges fused into the transposes (stores into
     the other ranks' buffers); all ranks in one process on one GPU, attached
     through device pointers, phases run rank after rank (a barrier between)."""
@@ -126,18 +156,16 @@ def test_p2p_phases_emulated_ranks(n1, n2, p, tdir, norm):
     xs = [torch.from_numpy(x[r * slab:(r + 1) * slab].copy()).to(DEV) for r in range(p)]
     outs = [torch.empty(slab, dtype=torch.complex64, device=DEV) for _ in range(p)]
     before = _lib.launch_counter()
-    for k in range(4):
+    for k in ((0, 1, 2, 3) if output_order == "natural" else (0, 1, 4)):
         for r in range(p):
             pl = plans[r]
-            pl.p2p_phase(k, xs[r].data_ptr() if k == 0 else 0, outs[r].data_ptr() if k == 3 else 0,
+            pl.p2p_phase(k, xs[r].data_ptr() if k == 0 else 0, outs[r].data_ptr() if k in (3, 4) else 0,
                          ws[r].data_ptr(), ws[r].numel(), st)
     y = torch.cat(outs).cpu().numpy()
     assert _lib.launch_counter() > before
-    xd = x.astype(np.complex128)
-    if tdir == "forward":
-        ref = np.fft.fft(xd, norm=norm if norm != "none" else "backward")
-    else:
-        ref = np.fft.ifft(xd, norm=norm if norm != "none" else "forward")
+    ref = _ref_transform(x, tdir, norm)
+    if output_order == "transposed":
+        ref = _transposed_ref(ref, n1, n2, p)
     assert rel_l2_per_transform(y, ref) <= TOL_F64, (n1, n2, p)
     with pytest.raises(ValueError):  # phases before attach are refused
         _lib.NativeDistPlan(n1, n2, p, 0).p2p_phase(1, 0, 0, ws[0].data_ptr(), ws[0].numel(), st)
@@ -170,6 +198,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+NCCL_CASES = [(1 << 22, "forward", "backward", "p2p", "natural"), (1 << 24, "inverse", "ortho", "p2p", "natural"),
+              (1 << 22, "forward", "backward", "nccl", "natural"), (1 << 24, "inverse", "ortho", "nccl", "natural"),
+              (1 << 22, "forward", "backward", "p2p", "transposed"),
+              (1 << 24, "inverse", "ortho", "nccl", "transposed")]
+
+
 def _nccl_rank(rank, world, port, results):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -178,19 +212,21 @@ def _nccl_rank(rank, world, port, results):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=datetime.timedelta(seconds=120))
     try:
-        cases = [(1 << 22, "forward", "backward", "p2p"), (1 << 24, "inverse", "ortho", "p2p"),
-                 (1 << 22, "forward", "backward", "nccl"), (1 << 24, "inverse", "ortho", "nccl")]
-        for idx, (n, tdir, norm, mode) in enumerate(cases):
+        for idx, (n, tdir, norm, mode, order) in enumerate(NCCL_CASES):
             rng = np.random.default_rng(idx % 2)
             x = cplx(rng, n)
             slab = n // world
-            f = bdist.DistributedFFT(n, transform_direction=tdir, norm=norm, device=dev, exchange=mode)
+            f = bdist.DistributedFFT(n, transform_direction=tdir, norm=norm, device=dev, exchange=mode,
+                                     output_order=order)
             assert f.exchange == mode
             f.execute(torch.from_numpy(x[rank * slab:(rank + 1) * slab].copy()).to(dev))  # twice: buffer reuse
             y = f.execute(torch.from_numpy(x[rank * slab:(rank + 1) * slab].copy()).to(dev)).cpu().numpy()
             xd = x.astype(np.complex128)
             ref = np.fft.fft(xd, norm=norm) if tdir == "forward" else np.fft.ifft(xd, norm=norm)
-            ref = ref[rank * slab:(rank + 1) * slab]
+            if order == "transposed":
+                ref = dist_oracle.transposed_slab(ref, f.n1, f.n2, world, rank)
+            else:
+                ref = ref[rank * slab:(rank + 1) * slab]
             results[(rank, idx)] = float(np.linalg.norm(y - ref) / np.linalg.norm(ref))
             first, count = bdist.batch_shard(8192)
             results[(rank, "shard")] = (first, count)
@@ -211,7 +247,7 @@ def test_distributed_fft_over_nccl():
                            start_method="spawn")
         res = dict(results)
     for r in range(world):
-        for idx in range(4):
+        for idx in range(len(NCCL_CASES)):
             assert res[(r, idx)] <= TOL_F64, (r, idx, res[(r, idx)])
     shards = sorted(res[(r, "shard")] for r in range(world))
     assert shards[0][0] == 0 and sum(c for _, c in shards) == 8192
