@@ -269,12 +269,12 @@ def choose_plan(n: int, b: int, tt: str = "c2c", td: str = "forward"):
                              params={"tile": half if half <= 4096 or (half <= 65536 and b >= 2) else 256,
                                      "rows": 1, "variant": "spread", "batch": b, "real_flow": real_flow},
                              transform_type=tt, transform_direction=td), "explicit"
-    # one CTA-resident pass up to 4096 points; 2^13..2^16 with a batch, the
+    # one CTA-resident pass up to 4096 points; 2^13..2^20 with a batch, the
     # fused single pass (tile = N); beyond, a 256-point local group and tail
     # passes of <= 2^9 points (every pass on the TMA-staged kernels); past 2^26
     # a 128-point local group (N = 2^30: 7 + 8 + 8 + 7 stages measured 1.5-2.5 %
     # faster than 8 + 8 + 7 + 7)
-    tile = n if n <= 4096 or (n <= 65536 and b >= 2) else (256 if n <= (1 << 26) else 128)
+    tile = n if n <= 4096 or (n <= (1 << 20) and b >= 2) else (256 if n <= (1 << 26) else 128)
     executed = "fft_dit_matrix_batch" if b > 1 else "fft_dit_matrix"
     return ExecutionPlan(n=n, batch=b, direction="dit", precision="fp32", selection_source="table",
                          reason="explicit B200 local-fused core (selector abstained: " + p.reason + ")",

@@ -157,7 +157,9 @@ def candidates(shape: Shape, space: DesignSpace | None = None) -> tuple[dict, li
                                     {"radix": 4, "variant": "spread", "batch": b})
         incumbents = [f"m4_spread_{d}", f"m4_folded_{d}"]
     for t in sp.matrix_tiles:
-        if t <= n and n % t == 0 and (t <= 4096 or (t == n and 13 <= l <= 16)):
+        # tile = N: one HBM round trip -- the fused single pass for 2^13..2^20
+        # with a batch, the cluster kernel for 2^13..2^16 at batch 1
+        if t <= n and n % t == 0 and (t <= 4096 or (t == n and (13 <= l <= 16 or (l <= 20 and b > 1)))):
             params = {"tile": t, "rows": 1}
             if b > 1:
                 params.update(variant="spread", batch=b)
@@ -622,6 +624,9 @@ def main(argv=None) -> int:
     m.add_argument("--trials", type=int, default=20)
     m.add_argument("--warmup", type=int, default=5)
     m.add_argument("--device", type=int, default=0)
+    m.add_argument("--only", nargs="+", default=None, metavar="KEY",
+                   help="measure only these shape keys (e.g. N1048576B16:dit:c2c-forward-backward); "
+                        "build merges runs, a later run re-measuring its shapes")
     b = sub.add_parser("build", help="build the selector table from run files")
     b.add_argument("runs", nargs="+")
     b.add_argument("--out", default=TABLE_PATH)
@@ -633,7 +638,14 @@ def main(argv=None) -> int:
     c.add_argument("--guard-pct", type=float, default=GUARD_PCT)
     a = ap.parse_args(argv)
     if a.cmd == "measure":
-        run = measure(default_shapes(a.quick), sessions=a.sessions, trials=a.trials, warmup=a.warmup,
+        shapes = default_shapes(a.quick)
+        if a.only:
+            known = {s.key for s in shapes}
+            unknown = [k for k in a.only if k not in known]
+            if unknown:
+                raise ConfigError(f"--only: not shapes of the size matrix: {', '.join(unknown)}")
+            shapes = [s for s in shapes if s.key in set(a.only)]
+        run = measure(shapes, sessions=a.sessions, trials=a.trials, warmup=a.warmup,
                       device=a.device, log=lambda s: print(s, file=sys.stderr, flush=True))
         save_run(run, a.out)
         return 0

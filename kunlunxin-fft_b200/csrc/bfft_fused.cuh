@@ -1,4 +1,4 @@
-// bfft_fused.cuh -- whole transforms of N = N1 * N2 points (2^13 .. 2^16) in
+// bfft_fused.cuh -- whole transforms of N = N1 * N2 points (2^13 .. 2^20) in
 // one HBM round trip, as one persistent kernel.
 //
 // Included by bfft_kernels.cu after bfft_pass_tma.cuh (it uses the TMA /
@@ -11,10 +11,9 @@
 //            written as one row n2 of a scratch slot S[n2][k1];
 //   phase B: N1 FFTs of N2 points over n2 for each k1 (columns of S), written
 //            to X[k1 + N1 k2] (out read as [k2][k1], k1 contiguous).
-// Both phases are tiles of K = 16 (or more, for short sub-FFTs) sub-FFTs
-// loaded by one TMA box into a dense [element][sub-FFT] shared tile -- the
-// column-pass geometry (PassTGeo) -- so the same tile is the landing buffer,
-// the Stockham exchange area and the store staging.
+// Both phases are tiles of K sub-FFTs (FusedTile: 8..64 columns) loaded by
+// TMA boxes into a dense [element][sub-FFT] shared tile, so the same tile is
+// the landing buffer, the Stockham exchange area and the store staging.
 //
 // The intermediate never goes to HBM on purpose: scratch slots form a ring of
 // S transforms (tens of MiB) whose stores and loads carry an L2 evict_last
@@ -37,17 +36,41 @@
 
 namespace bfft {
 
+// Tile of one phase: NC consumer threads, each carrying 16 elements of two
+// sub-FFTs (a pair); TF threads share a pair of L-point sub-FFTs, so a tile
+// holds K = 2 NC / TF sub-FFTs (columns) -- 16 for L = 256 with 128 consumers,
+// 8 for L = 1024 with 256.  Loaded by TMA boxes of K columns x LB elements into
+// a dense [element][column] stage (the landing buffer, the Stockham exchange
+// area and the store staging); ROWS 1 stages each output sub-FFT as a row
+// (padded) for one bulk copy each.
+template <int LOG2L, int ROWS, int NC>
+struct FusedTile {
+    static constexpr int L = 1 << LOG2L;
+    static constexpr int TF = L / 16;
+    static constexpr int NP = NC / TF;  // column pairs per tile
+    static constexpr int K = 2 * NP;
+    static constexpr int LB = L < 256 ? L : 256;  // TMA box extent along the element index
+    static constexpr int RPAD = ROWS ? 2 : 0;     // row staging: 16-byte aligned rows
+    static constexpr int SB = ((K * (L + RPAD) * 8) + 127) / 128 * 128;
+    // W_N column factors shared by the TF threads of a sub-FFT pair: [m][pair], 16 x NP
+    static constexpr bool COLTW = TF >= 4;
+    static constexpr int CPT = TF >= 16 ? 1 : 16 / TF;  // column factors per thread
+    static_assert(L >= 64 && NP >= 1 && K <= 256 && (K * 8) % 16 == 0, "fused tile geometry");
+};
+
+// 128 consumers (two CTAs per SM, 32 KiB stages) for sub-FFTs of <= 256
+// points (N = 2^13..2^16); 256 consumers (one CTA per SM, 64 KiB stages) when
+// a phase has 512- or 1024-point sub-FFTs (N = 2^17..2^20).
 template <int LA, int LB>
 struct FusedGeo {
-    using GA = PassTGeo<LA, 1>;  // phase A: column FFTs of N1, rows out (bulk copies)
-    using GB = PassTGeo<LB, 0>;  // phase B: column FFTs of N2 over the slot, columns out (TMA store)
+    static constexpr bool WIDE = LA > 8 || LB > 8;
+    static constexpr int CONSUMERS = WIDE ? 256 : 128;
+    using GA = FusedTile<LA, 1, CONSUMERS>;  // phase A: column FFTs of N1, rows out (bulk copies)
+    using GB = FusedTile<LB, 0, CONSUMERS>;  // phase B: column FFTs of N2 over the slot, columns out (TMA store)
     static constexpr int N1 = 1 << LA, N2 = 1 << LB;
-    // consumers carry two columns each (paired FP32x2 arithmetic): half the
-    // threads of the column-tile geometry
-    static constexpr int CONSUMERS = 128;
     static constexpr int THREADS = CONSUMERS + 64;  // + the loader and the storer warps
-    static_assert(GA::THREADS == 2 * CONSUMERS && GB::THREADS == 2 * CONSUMERS, "256-lane column tiles");
-    static constexpr int NPA = GA::K / 2, NPB = GB::K / 2;  // column pairs per tile
+    static constexpr int MINB = WIDE ? 1 : 2;
+    static constexpr int NPA = GA::NP, NPB = GB::NP;  // column pairs per tile
     static constexpr int SB = GA::SB > GB::SB ? GA::SB : GB::SB;
     static constexpr int STAGES = 3;
     static constexpr int TA = N2 / GA::K;  // phase-A tiles per transform
@@ -61,6 +84,7 @@ struct FusedGeo {
     // shared memory, so the launcher may raise the dynamic limit to the full 227 KiB
     static constexpr int CTRL = 256;
     static constexpr size_t SMEM = 128 + (size_t)STAGES * SB + CTRL + (size_t)(TWA + TWB + COLTW) * sizeof(CPair);
+    static_assert(SMEM <= 220 * 1024, "fused stages");
 };
 
 __device__ __forceinline__ uint64_t policy_evict_first() {
@@ -132,10 +156,11 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
 
-// Warp-specialised: warps 0-7 (the consumers) compute tiles and meet only at
-// named barrier 1; lane 0 of warp 8 (the loader) claims tickets, waits on
-// dependencies and starts the TMA loads; lane 0 of warp 9 (the storer) stores
-// finished tiles and publishes them.  Consumers never wait for a global
+// Warp-specialised: the consumer warps (threads 0 .. CONSUMERS-1) compute
+// tiles and meet only at named barrier 1; lane 0 of the next warp (the
+// loader) claims tickets, waits on dependencies and starts the TMA loads;
+// lane 0 of the last warp (the storer) stores finished tiles and publishes
+// them.  Consumers never wait for a global
 // atomic or a store to complete.  The q-th item of the CTA uses stage q % ST:
 //   full[s]   loader    -> consumers, storer: the tile landed (s_item[s] set);
 //   staged[s] consumers -> storer: the results are staged in the stage;
@@ -146,7 +171,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
 // loader, and the loader may block on a dependency (always an earlier ticket)
 // without closing a cycle.
 template <int LA, int LB>
-__global__ void __launch_bounds__(FusedGeo<LA, LB>::THREADS, 2)
+__global__ void __launch_bounds__(FusedGeo<LA, LB>::THREADS, FusedGeo<LA, LB>::MINB)
     k_fused_fft(const __grid_constant__ CUtensorMap ta_in, const __grid_constant__ CUtensorMap tb_in,
                 const __grid_constant__ CUtensorMap tb_out, FusedArgs a) {
     using G = FusedGeo<LA, LB>;
@@ -337,7 +362,7 @@ __global__ void __launch_bounds__(FusedGeo<LA, LB>::THREADS, 2)
     }
     if (tid >= NC) return;
 
-    // ==================================================== consumers (128 threads, a column pair each)
+    // ==================================================== consumers (a column pair per TF threads)
     const u64 zero = 0;
     const u64 sre = f2splat(a.scale), sim = f2splat(a.conj_out ? -a.scale : a.scale);
     const bool scaled = a.scale != 1.0f || a.conj_out;
@@ -458,35 +483,45 @@ static cudaError_t launch_fused_t(const float2* in, float2* out, const FusedArgs
 }
 
 // Scratch ring sizing, in tickets (the tiles of one transform form one round
-// of TA + TB tickets; a ticket stands for 16 KiB of ring): phase-B tiles come
-// up kLagTickets after their transform's phase-A tiles, and a slot is reused
-// kSlackTickets after its phase-B tiles came up, so S > D.  Measured on B200
-// (N = 2^16, B = 8192; N = 2^13, B = 65536): lag/slack 768/768 leaves the
-// loaders blocked on dependencies (2.96 ms), 1024/1024 2.69 ms, 1536/1536
-// 2.56 ms (a 48 MiB ring), 2048/2048 2.82 ms and 3072/1536 2.98 ms -- the
-// larger rings no longer stay in L2.
+// of TA + TB tickets): phase-B tiles come up kLagTickets after their
+// transform's phase-A tiles, and a slot is reused kSlackTickets after its
+// phase-B tiles came up, so S > D.  A ticket stands for 16 KiB of ring with
+// 128 consumers and 32 KiB with 256 (N >= 2^17), so the ring is 48 MiB either
+// way.  Measured on B200 (N = 2^16, B = 8192; N = 2^13, B = 65536): lag/slack
+// 768/768 leaves the loaders blocked on dependencies (2.96 ms), 1024/1024
+// 2.69 ms, 1536/1536 2.56 ms (a 48 MiB ring), 2048/2048 2.82 ms and 3072/1536
+// 2.98 ms -- the larger rings no longer stay in L2.
 constexpr int kLagTickets = 1536, kSlackTickets = 1536;
 
-inline int fused_round_len(int log2n) {
+inline void fused_round(int log2n, int* round_len, int* ticket_kib) {
     switch (log2n) {
-        case 13: return FusedGeo<7, 6>::TA + FusedGeo<7, 6>::TB;
-        case 14: return FusedGeo<7, 7>::TA + FusedGeo<7, 7>::TB;
-        case 15: return FusedGeo<8, 7>::TA + FusedGeo<8, 7>::TB;
-        default: return FusedGeo<8, 8>::TA + FusedGeo<8, 8>::TB;
+        case 13: *round_len = FusedGeo<7, 6>::TA + FusedGeo<7, 6>::TB; break;
+        case 14: *round_len = FusedGeo<7, 7>::TA + FusedGeo<7, 7>::TB; break;
+        case 15: *round_len = FusedGeo<8, 7>::TA + FusedGeo<8, 7>::TB; break;
+        case 16: *round_len = FusedGeo<8, 8>::TA + FusedGeo<8, 8>::TB; break;
+        case 17: *round_len = FusedGeo<9, 8>::TA + FusedGeo<9, 8>::TB; break;
+        case 18: *round_len = FusedGeo<9, 9>::TA + FusedGeo<9, 9>::TB; break;
+        case 19: *round_len = FusedGeo<10, 9>::TA + FusedGeo<10, 9>::TB; break;
+        default: *round_len = FusedGeo<10, 10>::TA + FusedGeo<10, 10>::TB; break;
     }
+    *ticket_kib = (int)(((int64_t(8) << log2n) / 1024) / *round_len);
 }
 
 inline void fused_ring(int64_t n, int64_t batch, int* slots, int* lag) {
     int log2n = 0;
     while ((int64_t(1) << log2n) < n) ++log2n;
-    const int rl = fused_round_len(log2n);
-    const int D = (kLagTickets + rl - 1) / rl;
-    const int64_t want = D + (kSlackTickets + rl - 1) / rl;
+    int rl = 0, kib = 16;
+    fused_round(log2n, &rl, &kib);
+    // the same ring bytes whatever the ticket size
+    const int lag_t = kib > 16 ? kLagTickets * 16 / kib : kLagTickets;
+    const int slack_t = kib > 16 ? kSlackTickets * 16 / kib : kSlackTickets;
+    const int D = (lag_t + rl - 1) / rl;
+    const int64_t want = D + (slack_t + rl - 1) / rl;
     *lag = D;
     *slots = (int)(batch < want ? batch : want);  // batch <= S: no slot is reused
 }
 
-bool fused_supported(int log2n) { return log2n >= 13 && log2n <= 16; }
+bool fused_supported(int log2n) { return log2n >= 13 && log2n <= 20; }
 
 size_t fused_workspace_bytes(int64_t n, int64_t batch) {
     int slots = 0, lag = 0;
@@ -509,6 +544,10 @@ cudaError_t launch_fused_fft(int log2n, const float2* in, float2* out, void* wor
         case 14: return launch_fused_t<7, 7>(in, out, a, s);
         case 15: return launch_fused_t<8, 7>(in, out, a, s);
         case 16: return launch_fused_t<8, 8>(in, out, a, s);
+        case 17: return launch_fused_t<9, 8>(in, out, a, s);
+        case 18: return launch_fused_t<9, 9>(in, out, a, s);
+        case 19: return launch_fused_t<10, 9>(in, out, a, s);
+        case 20: return launch_fused_t<10, 10>(in, out, a, s);
         default: return cudaErrorInvalidValue;
     }
 }

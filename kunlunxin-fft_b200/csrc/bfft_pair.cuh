@@ -11,7 +11,7 @@
 // running the same operation sequence would.
 //
 // Included by bfft_kernels.cu (uses the unit twiddle levels and the Stockham
-// pass shapes: radix_log2, tw_offset, tw_total).
+// pass shapes: radix_log2, tw_split, tw_offset, tw_total).
 #pragma once
 
 namespace bfft {
@@ -155,17 +155,27 @@ struct PairDft<2> {
 };
 
 // Pair twiddle tables of the Stockham passes: the entries of tw_offset /
-// tw_total (row k of pass p holds W_{Rp}^{j k}, j = 1..R-1), each stored as
-// (wr, wr, wi, wi) so one 16-byte load gives the pair operand.  Only the
-// unsplit passes (L <= 4096 without the pass-2 split, i.e. L <= 256 here).
+// tw_total (row k of pass p holds W_{Rp}^{j k}, j = 1..R-1; pass 2 of radix
+// R >= 4 the split rows kl then kh, W_{256 R}^{j kl} and W_{16 R}^{j kh}),
+// each stored as (wr, wr, wi, wi) so one 16-byte load gives the pair operand.
+// Sub-FFTs of up to 1024 points (three passes).
 template <int LOG2L>
 __device__ __forceinline__ void fill_pair_twiddles(CPair* tw) {
     constexpr int NP = LOG2L <= 4 ? 1 : (LOG2L + 3) / 4;
-    static_assert(NP <= 2, "pair passes: sub-FFTs of at most 256 points");
+    static_assert(NP <= 3, "pair passes: sub-FFTs of at most 4096 points");
     for (int pass = 1; pass < NP; ++pass) {
         const int r = 1 << radix_log2(LOG2L, pass), p = 1 << (4 * pass);
-        const float2* lvl = g_tw_levels + r * p;
         CPair* dst = tw + tw_offset(LOG2L, pass);
+        if (tw_split(LOG2L, pass)) {
+            const int cnt = 2 * 16 * (r - 1);
+            for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+                const int row = i / (r - 1), j = i - row * (r - 1) + 1;
+                const float2 w = row < 16 ? g_tw_levels[r * p + j * row] : g_tw_levels[r * 16 + j * (row - 16)];
+                dst[i] = CPair{f2splat(w.x), f2splat(w.y)};
+            }
+            continue;
+        }
+        const float2* lvl = g_tw_levels + r * p;
         const int cnt = p * (r - 1);
         for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
             const int k = i / (r - 1), j = i - k * (r - 1) + 1;
@@ -195,7 +205,12 @@ __device__ __forceinline__ void pair_passes(CPair (&v)[16], int t, ulonglong2* r
             CPair u[R];
 #pragma unroll
             for (int j = 0; j < R; ++j) u[j] = v[q + j * NB];
-            if constexpr (PASS > 0) {
+            if constexpr (tw_split(LOG2L, PASS)) {  // W_{256 R}^{j k} = W_{256 R}^{j kl} W_{16 R}^{j kh}
+                const CPair* tl = tw + tw_offset(LOG2L, PASS) + (k & 15) * (R - 1) - 1;
+                const CPair* th = tw + tw_offset(LOG2L, PASS) + (16 + (k >> 4)) * (R - 1) - 1;
+#pragma unroll
+                for (int j = 1; j < R; ++j) u[j] = cp_mul(u[j], cp_mul(tl[j], th[j]));
+            } else if constexpr (PASS > 0) {
                 const CPair* w = tw + tw_offset(LOG2L, PASS) + k * (R - 1) - 1;
 #pragma unroll
                 for (int j = 1; j < R; ++j) u[j] = cp_mul(u[j], w[j]);

@@ -397,19 +397,19 @@ def test_batch_shard_config_full_size(tile):
     assert _lib.device_status(0) == 0
 
 
-@pytest.mark.parametrize("log2n", [13, 14, 15, 16])
+@pytest.mark.parametrize("log2n", [13, 14, 15, 16, 17, 18, 19, 20])
 def test_fused_single_pass_batches_and_ring_reuse(log2n):
     """The fused single pass (tile = N, batch >= 2): ragged batches, and a batch
-    past the scratch ring so slots are reused (the ring holds 3072 tickets of
-    16 KiB: 96 transforms at 2^16 .. 768 at 2^13); forward against float64 on
-    every row, inverse with ortho norm against float64, one launch per call,
-    and no bounded wait expired."""
+    past the scratch ring so slots are reused (the ring holds 48 MiB: 96
+    transforms at 2^16 .. 768 at 2^13, 6 at 2^20 with the 256-consumer tiles);
+    forward against float64 on every row, inverse with ortho norm against
+    float64, one launch per call, and no bounded wait expired."""
     from bfft.entry import native_plan_for
 
     n = 1 << log2n
     ring = 3072 * 16384 // (8 * n)
     rng = np.random.default_rng(100 + log2n)
-    for b in (2, 3, 37, ring + 45):
+    for b in ((2, 3, 37, ring + 45) if log2n <= 16 else (2, 3, ring + 5)):
         x = cplx(rng, (b, n))
         t = dev(x)
         p = _plan("fft_dit_matrix_batch", n, b, params={"tile": n})

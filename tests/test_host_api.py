@@ -181,7 +181,7 @@ def test_plan_through_b200_table(tmp_path):
 
 @pytest.mark.parametrize("mutate, needle", [
     (lambda e: e.update(block=100), "block"),
-    (lambda e: e["params"].update(tile=131072), "tile"),
+    (lambda e: e["params"].update(tile=1 << 21), "tile"),
     (lambda e: e["params"].update(variant="diagonal"), "variant"),
     (lambda e: e.update(executed="fft_dit"), "executed"),
     (lambda e: e.update(processing_unit="tensor-core"), "processing"),

@@ -43,8 +43,10 @@ def test_candidate_enumeration_matches_the_design_space():
     assert "m1_t64" in c and "m2_dit_t2048" in c and "m2_dit_t4096" not in c
     c, inc = TB.candidates(TB.Shape(65536, 1, "dif"))
     assert "m2_dif_t65536" in c and not any(k.startswith("m1_") for k in c)  # cluster tile, no DIF M1
-    c, inc = TB.candidates(TB.Shape(1 << 20, 16, "dit"))
-    assert inc == ["m4_spread_dit", "m4_folded_dit"] and "m2_dit_t1024" in c and "m2_dit_t1048576" not in c
+    c, inc = TB.candidates(TB.Shape(1 << 20, 16, "dit"))  # the fused single pass (tile = N) with a batch
+    assert inc == ["m4_spread_dit", "m4_folded_dit"] and "m2_dit_t1024" in c and "m2_dit_t1048576" in c
+    c, _ = TB.candidates(TB.Shape(1 << 20, 1, "dit"))  # no single-pass kernel for one 2^20 transform
+    assert "m2_dit_t1024" in c and "m2_dit_t1048576" not in c
     c, inc = TB.candidates(TB.Shape(4096, 256, "dit", "r2c", "forward", "backward", True))
     assert inc == ["m4_folded_dit"] and c["h_dif_t2048"]["executed"] == "fft_dif_matrix_batch"
     c, _ = TB.candidates(TB.Shape(2048, 16, "dit"))
