@@ -369,10 +369,11 @@ __global__ void __launch_bounds__(FusedGeo<LA, LB>::THREADS, FusedGeo<LA, LB>::M
     for (int64_t q = 0;; ++q) {
         const int s = (int)(q % ST);
         const bool ok = mbar_wait_bounded(&full[s], (uint32_t)((q / ST) & 1));
+        // one decision for all consumers (the flag may change between their reads)
+        const bool stop = group_sync_or<NC>(!ok || *s_abort);
         if (!ok) *s_abort = 1;
-        group_sync<NC>();
         const FusedItem cur = s_item[s];
-        if (cur.kind == 0 || *s_abort) break;
+        if (cur.kind == 0 || stop) break;
         float2* buf = stage(s);
         const float4* buf4 = reinterpret_cast<const float4*>(buf);
         if (cur.kind == 1) {

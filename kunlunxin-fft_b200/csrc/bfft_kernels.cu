@@ -540,6 +540,23 @@ __device__ __forceinline__ void group_sync() {
     if constexpr (NBAR == 0) __syncthreads();
     else asm volatile("bar.sync 1, %0;" ::"n"(NBAR) : "memory");
 }
+// The same barrier, returning the OR of `pred` over its threads: one decision
+// that every participant sees alike.
+template <int NBAR>
+__device__ __forceinline__ bool group_sync_or(bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n"
+        " .reg .pred p, q;\n"
+        " setp.ne.u32 p, %1, 0;\n"
+        " bar.red.or.pred q, 1, %2, p;\n"
+        " selp.u32 %0, 1, 0, q;\n"
+        "}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "n"(NBAR)
+        : "memory");
+    return r != 0;
+}
 
 template <int LOG2L, int PASS, int E, int TF, int XS = 0, bool PK = false, int NBAR = 0>
 __device__ __forceinline__ void stockham_passes(float2 (&v)[E], int t, float2* region, const float2* tw_smem) {
@@ -961,6 +978,7 @@ static cudaError_t launch_pass_l(int layout, int lmap, int smap, const float2* i
 #include "bfft_pass_tma.cuh"
 #include "bfft_pair.cuh"
 #include "bfft_fused.cuh"
+#include "bfft_rows_pair.cuh"
 #include "bfft_tc.cuh"
 
 namespace bfft {
@@ -1203,6 +1221,8 @@ cudaError_t launch_pass(int log2l, int layout, int lmap, int smap, const float2*
         if (e != cudaErrorNotSupported) return e;
     } else if (smap != 2) {  // row tiles with row outputs: bulk-copy pass when the shape allows it
         cudaError_t e = log2l == 1 ? launch_rows_regs(log2l, in, out, a, s) : launch_rows_shfl(log2l, in, out, a, s);
+        if (e != cudaErrorNotSupported) return e;
+        e = launch_rows_pair(log2l, in, out, a, s);
         if (e != cudaErrorNotSupported) return e;
         e = launch_pass_tma_rows(log2l, in, out, a, s);
         if (e != cudaErrorNotSupported) return e;
