@@ -192,13 +192,19 @@ __device__ __forceinline__ void fill_pair_twiddles(CPair* tw) {
 // 16 b + j, 256 bytes apart for consecutive b, so without it the lanes of a
 // warp meet on the same four banks (32-way conflicts with one pair per
 // index); with it, 8 consecutive b fill a whole bank row.  The later passes'
-// stores and every read (consecutive indices) stay conflict-free.
-__device__ __forceinline__ int pair_swizzle(int i) { return i ^ ((i >> 4) & 7); }
+// stores and every read (consecutive indices) stay conflict-free.  With 8 or
+// more pairs per index an index is a whole bank row already: no swizzle (its
+// index arithmetic would only cost instructions).
+template <int NPAIR>
+__device__ __forceinline__ int pair_swizzle(int i) {
+    if constexpr (NPAIR >= 8) return i;
+    else return i ^ ((i >> 4) & 7);
+}
 
 // Stockham passes on pairs: the structure of stockham_passes (butterfly b
 // of the thread takes slots q + j NB, output j goes to (b/p) p R + (b mod p)
 // + j p), the exchange area holding pair i of the thread's column pair at
-// region[pair_swizzle(i) * NPAIR] (16 bytes each).  NBAR threads meet at named barrier 1.
+// region[pair_swizzle<NPAIR>(i) * NPAIR] (16 bytes each).  NBAR threads meet at named barrier 1.
 template <int LOG2L, int PASS, int TF, int NPAIR, int NBAR>
 __device__ __forceinline__ void pair_passes(CPair (&v)[16], int t, ulonglong2* region, const CPair* tw) {
     constexpr int E = 16;
@@ -238,13 +244,13 @@ __device__ __forceinline__ void pair_passes(CPair (&v)[16], int t, ulonglong2* r
 #pragma unroll
                 for (int j = 0; j < R; ++j) {
                     const CPair x = v[q + j * NB];
-                    region[pair_swizzle(base + (j << LP)) * NPAIR] = make_ulonglong2(x.re, x.im);
+                    region[pair_swizzle<NPAIR>(base + (j << LP)) * NPAIR] = make_ulonglong2(x.re, x.im);
                 }
             }
             group_sync<NBAR>();
 #pragma unroll
             for (int m = 0; m < E; ++m) {
-                const ulonglong2 x = region[pair_swizzle(t + m * TF) * NPAIR];
+                const ulonglong2 x = region[pair_swizzle<NPAIR>(t + m * TF) * NPAIR];
                 v[m] = CPair{x.x, x.y};
             }
             group_sync<NBAR>();
