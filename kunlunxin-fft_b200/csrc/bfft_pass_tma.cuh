@@ -37,6 +37,15 @@ constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+// `p` (a pointer into dynamic shared memory) rounded up to an A-byte boundary
+// by pointer arithmetic, so the result keeps its shared-memory provenance and
+// the compiler emits shared-memory loads and stores (LDS / STS) through it.
+// (Rounding through an integer cast loses that: every access through the
+// result became a generic load or store, tracked by the long scoreboard.)
+template <int A>
+__device__ __forceinline__ unsigned char* align_smem(unsigned char* p) {
+    return p + ((A - (smem_u32(p) & (A - 1))) & (A - 1));
+}
 __device__ __forceinline__ uint64_t global_timer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -62,15 +71,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread may sleep until the phase
+// completes or about `hint_ns` pass, instead of spinning on the barrier (a
+// spinning producer warp takes issue slots from the computing warps).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* b, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        " .reg .pred p;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
 // Wait for phase `parity` of `b` to complete; false (and status bit 0) when
 // it has not completed within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* b, uint32_t parity) {
     if (mbar_try_wait(b, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (;;) {
-#pragma unroll 1
-        for (int i = 0; i < 64; ++i)
-            if (mbar_try_wait(b, parity)) return true;
+        if (mbar_try_wait_sleep(b, parity, 20000u)) return true;
         if (global_timer_ns() - t0 > kWaitLimitNs) {
             atomicOr(&g_kernel_status, 1u);
             return false;
@@ -166,8 +189,7 @@ __global__ void __launch_bounds__(PassTGeo<LOG2L, ROWS>::THREADS, PassTGeo<LOG2L
                float2* __restrict__ out, PassArgs a) {
     using G = PassTGeo<LOG2L, ROWS>;
     extern __shared__ unsigned char smem_raw[];
-    unsigned char* base =
-        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    unsigned char* base = align_smem<128>(smem_raw);
     uint64_t* full = reinterpret_cast<uint64_t*>(base + G::STAGES * G::SB);
     float2* tw_smem = reinterpret_cast<float2*>(full + 8);
     float2* coltw = tw_smem + tw_total(LOG2L);
@@ -350,8 +372,7 @@ __global__ void __launch_bounds__(PassRGeo<LOG2L>::THREADS, PassRGeo<LOG2L>::MIN
                     int out_contig) {
     using G = PassRGeo<LOG2L>;
     extern __shared__ unsigned char smem_raw[];
-    unsigned char* base =
-        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    unsigned char* base = align_smem<128>(smem_raw);
     uint64_t* full = reinterpret_cast<uint64_t*>(base + G::STAGES * G::SB);
     float2* tw_smem = reinterpret_cast<float2*>(full + 8);
     auto stage = [&](int s) { return reinterpret_cast<float2*>(base + s * G::SB); };

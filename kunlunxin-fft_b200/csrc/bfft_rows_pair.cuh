@@ -64,8 +64,7 @@ __global__ void __launch_bounds__(RowsPairGeo<LOG2L>::THREADS, RowsPairGeo<LOG2L
     constexpr int NC = G::CONSUMERS;
     static_assert(8 * 3 * ST + sizeof(int) <= G::CTRL, "control block");
     extern __shared__ unsigned char smem_raw[];
-    unsigned char* base =
-        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    unsigned char* base = align_smem<128>(smem_raw);
     unsigned char* ctrl = base + ST * G::SB;
     uint64_t* full = reinterpret_cast<uint64_t*>(ctrl);
     uint64_t* staged = full + ST;

@@ -102,8 +102,7 @@ __global__ void __launch_bounds__(TcGeo::THREADS)
                     int64_t rows, float scale, int conj_in, int conj_out) {
     using G = TcGeo;
     extern __shared__ unsigned char smem_raw[];
-    unsigned char* base =
-        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* base = align_smem<1024>(smem_raw);
     unsigned char* buf = base;  // TMA landing tile, then Ah in place, then the output staging
     unsigned char* al = base + G::TILE;
     unsigned char* bh = base + 2 * G::TILE;
