@@ -60,13 +60,13 @@ METRIC = "complex64 C2C FFT GFLOP/s (5N\u00b7log2N/t) and HBM GB/s vs roofline, 
 # processed; configs 3 and 4 captured at their full size.  Keyed by workload
 # and transform length.
 PROFILED_TRAFFIC = {
-    ("5a", 65536): (10.31e9, "k_fused_fft<8,8>: 291.5 + 353.1 MB at B=512, scaled x16"),
+    ("5a", 65536): (10.21e9, "k_fused_fft<8,8>: 291.2 + 346.9 MB at B=512, scaled x16"),
     ("sweep", 2): (217.6e6, "k_rows_regs<1>"), ("sweep", 16): (215.2e6, "k_rows_shfl<4>"),
     ("sweep", 64): (217.7e6, "k_rows_shfl<6>"), ("sweep", 128): (215.0e6, "k_rows_shfl128"),
-    ("sweep", 256): (214.3e6, "k_pass_tma_rows<8>"), ("sweep", 1024): (218.0e6, "k_pass_tma_rows<10>"),
-    ("sweep", 4096): (221.4e6, "k_pass_tma_rows<12>"), ("sweep", 8192): (280.2e6, "k_fused_fft<7,6>"),
-    ("sweep", 32768): (289.8e6, "k_fused_fft<8,7>"), ("sweep", 131072): (220.9e6, "k_pass_tma<9,0,0>"),
-    ("sweep", 1048576): (219.5e6, "k_pass_tma<7,0,0>"),
+    ("sweep", 256): (214.0e6, "k_rows_pair<8>"), ("sweep", 1024): (214.2e6, "k_rows_pair<10>"),
+    ("sweep", 4096): (215.9e6, "k_rows_pair<12>"), ("sweep", 8192): (279.3e6, "k_fused_fft<7,6>"),
+    ("sweep", 32768): (289.8e6, "k_fused_fft<8,7>"), ("sweep", 131072): (287.4e6, "k_fused_fft<9,8>"),
+    ("sweep", 1048576): (291.0e6, "k_fused_fft<10,10>"),
     ("c4-r2c", 65536): (111.1e6, "k_fused_fft<8,7> (the core)"), ("c4-c2r", 65536): (111.5e6, "k_fused_fft<8,7>"),
 }
 FALLBACK_HBM_GBS = 6650.0
@@ -508,8 +508,12 @@ def run_batch(args, wl, ctx) -> dict:
     # per launch on this rank (b of the workload's rows), like `achieved`
     traffic_src = traffic[1] if traffic is not None and args.batch is None else None
     traffic = traffic[0] * b / wl["batch"] if traffic is not None and args.batch is None else None
-    kernel = ("k_fused_fft (fused single pass)" if native.launches == 1 and n > 4096 and tt == "c2c"
-              else "k_pass_tma / k_pass_tma_rows / k_rows_shfl (CTA-resident Stockham passes)")
+    if native.launches == 1 and n > 4096 and tt == "c2c":
+        kernel = "k_fused_fft (fused single pass)"
+    elif native.launches == 1 and n in (256, 1024, 2048, 4096) and tt == "c2c":
+        kernel = "k_rows_pair (warp-specialised paired row FFT)"
+    else:
+        kernel = "k_pass_tma / k_pass_tma_rows / k_rows_shfl (CTA-resident Stockham passes)"
     roofline = {"bound": "hbm", "kernel": kernel, "achieved": achieved,
                 "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
                 "traffic": traffic, "traffic_source": traffic_src, "launches_per_step": native.launches,
