@@ -288,6 +288,14 @@ BFFT_EXPORT bfft_status bfft_stream_plan_destroy(bfft_stream_plan_t plan);
  * word.  Always 0 in a healthy run -- the tests check it. */
 BFFT_EXPORT bfft_status bfft_device_status(int32_t device, uint32_t* status, int32_t clear);
 
+/* Failure-detection probe (no reference counterpart: the reference has no
+ * device-side waits).  Runs one kernel on `stream` whose two bounded waits --
+ * on an mbarrier nothing arrives on, then on a dependency counter nothing
+ * increments -- each give up after their limit (about 1 s) and set status
+ * bits 0 and 1; synchronises the stream and returns BFFT_OK.  Read and clear
+ * the bits with bfft_device_status.  Takes about 2 s. */
+BFFT_EXPORT bfft_status bfft_probe_bounded_waits(int32_t device, void* stream);
+
 /* Total kernels this library has enqueued in this process (all devices). */
 BFFT_EXPORT uint64_t bfft_launch_counter(void);
 

@@ -32,6 +32,7 @@ EXPORTS = ("bfft_api_version", "bfft_last_error", "bfft_plan_create", "bfft_plan
            "bfft_index_map", "bfft_launch_counter", "bfft_hybrid_c2c_noalloc", "bfft_tc_dft16_rows",
            "bfft_dist_batch_shard", "bfft_dist_plan_create", "bfft_dist_workspace_size",
            "bfft_dist_phase", "bfft_dist_plan_launches", "bfft_dist_plan_destroy", "bfft_device_status",
+           "bfft_probe_bounded_waits",
            "bfft_stream_plan_create", "bfft_stream_plan_info", "bfft_stream_execute", "bfft_stream_plan_destroy",
            "bfft_dist_p2p_prepare", "bfft_dist_p2p_attach", "bfft_dist_p2p_attach_pointers", "bfft_dist_p2p_phase")
 
@@ -93,6 +94,7 @@ def load() -> ctypes.CDLL:
         L.bfft_dist_plan_launches.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_int)]
         L.bfft_dist_plan_destroy.argtypes = [vp]
         L.bfft_device_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint32), i32]
+        L.bfft_probe_bounded_waits.argtypes = [i32, vp]
         L.bfft_stream_plan_create.argtypes = [ctypes.POINTER(PlanDesc), i64, ctypes.POINTER(vp)]
         L.bfft_stream_plan_info.argtypes = [vp, ctypes.POINTER(sz), ctypes.POINTER(sz), ctypes.POINTER(ctypes.c_int)]
         L.bfft_stream_execute.argtypes = [vp, vp, vp, vp]

@@ -936,6 +936,16 @@ bfft_status bfft_device_status(int32_t device, uint32_t* status, int32_t clear) 
     return BFFT_OK;
 }
 
+bfft_status bfft_probe_bounded_waits(int32_t device, void* stream) {
+    DeviceGuard g(device);
+    if (!g.ok) return fail(BFFT_ERR_CUDA, "cannot select device %d", device);
+    cudaStream_t s = (cudaStream_t)stream;
+    cudaError_t e = run_wait_probe(s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "probe_bounded_waits");
+    return BFFT_OK;
+}
+
 bfft_status bfft_tc_dft16_rows(const void* in, void* out, int64_t rows, int32_t transform_direction, float scale,
                                int32_t device, void* stream) {
     if (!in || !out) return fail(BFFT_ERR_VALUE, "null pointer");

@@ -983,6 +983,26 @@ static cudaError_t launch_pass_l(int layout, int lmap, int smap, const float2* i
 
 namespace bfft {
 
+// Failure-detection probe: one thread waits, through the same bounded waits the
+// kernels use, on an mbarrier that nothing arrives on and on a counter that
+// nothing increments.  Each wait gives up after kWaitLimitNs, records its bit
+// in the status word (0: mbarrier, 1: dependency counter) and the kernel
+// returns normally -- the context stays usable.
+__device__ uint32_t g_probe_counter;  // never incremented
+
+__global__ void k_wait_probe() {
+    __shared__ uint64_t bar;
+    mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    (void)mbar_wait_bounded(&bar, 0);
+    (void)counter_wait_bounded(&g_probe_counter, 1u);
+}
+
+cudaError_t run_wait_probe(cudaStream_t s) {
+    k_wait_probe<<<1, 1, 0, s>>>();
+    return cudaGetLastError();
+}
+
 cudaError_t read_device_status(unsigned* status, bool clear) {
     cudaError_t e = cudaMemcpyFromSymbol(status, g_kernel_status, sizeof(unsigned));
     if (e == cudaSuccess && clear) {

@@ -90,6 +90,8 @@ cudaError_t launch_fused_fft(int log2n, const float2* in, float2* out, void* wor
 // Status word the kernels set when a bounded wait expires (bit 0: an
 // mbarrier wait of the TMA pass); read synchronously, optionally cleared.
 cudaError_t read_device_status(unsigned* status, bool clear);
+// One kernel whose two bounded waits (mbarrier, dependency counter) expire.
+cudaError_t run_wait_probe(cudaStream_t s);
 
 // SM count of `dev`, cached after the first query (thread-safe).
 // 16-point DFT of each contiguous row of `rows` x 16 complex64 on the tensor
