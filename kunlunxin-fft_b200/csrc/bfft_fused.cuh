@@ -490,8 +490,16 @@ static cudaError_t launch_fused_t(const float2* in, float2* out, const FusedArgs
 // way.  Measured on B200 (N = 2^16, B = 8192; N = 2^13, B = 65536): lag/slack
 // 768/768 leaves the loaders blocked on dependencies (2.96 ms), 1024/1024
 // 2.69 ms, 1536/1536 2.56 ms (a 48 MiB ring), 2048/2048 2.82 ms and 3072/1536
-// 2.98 ms -- the larger rings no longer stay in L2.
+// 2.98 ms -- the larger rings no longer stay in L2.  After the kernel got
+// faster (shared-memory accesses as such, sleeping waits) the optimum moved
+// for long runs: N = 2^16, B = 8192 (4 GiB) takes 2.29 ms at 1280/1280 (a
+// 40 MiB ring) against 2.36 ms at 1536/1536 (1152/1152 2.33, 1280/1024 2.31,
+// 1024/1024 2.40, 1792/1792 2.53), while a 128 MiB batch (B N = 2^24) stays
+// faster at 1536/1536 (N = 2^13: 99-102 against 105 us; N = 2^16: 97 against
+// 103 us).  Batches of 2^26 points (512 MiB) or more use the smaller ring.
 constexpr int kLagTickets = 1536, kSlackTickets = 1536;
+constexpr int kLagTicketsLong = 1280, kSlackTicketsLong = 1280;
+constexpr int64_t kLongRunPoints = int64_t(1) << 26;
 
 inline void fused_round(int log2n, int* round_len, int* ticket_kib) {
     switch (log2n) {
@@ -512,9 +520,12 @@ inline void fused_ring(int64_t n, int64_t batch, int* slots, int* lag) {
     while ((int64_t(1) << log2n) < n) ++log2n;
     int rl = 0, kib = 16;
     fused_round(log2n, &rl, &kib);
+    const bool long_run = n * batch >= kLongRunPoints;
+    const int lag0 = long_run ? kLagTicketsLong : kLagTickets;
+    const int slack0 = long_run ? kSlackTicketsLong : kSlackTickets;
     // the same ring bytes whatever the ticket size
-    const int lag_t = kib > 16 ? kLagTickets * 16 / kib : kLagTickets;
-    const int slack_t = kib > 16 ? kSlackTickets * 16 / kib : kSlackTickets;
+    const int lag_t = kib > 16 ? lag0 * 16 / kib : lag0;
+    const int slack_t = kib > 16 ? slack0 * 16 / kib : slack0;
     const int D = (lag_t + rl - 1) / rl;
     const int64_t want = D + (slack_t + rl - 1) / rl;
     *lag = D;
