@@ -478,11 +478,13 @@ def test_installed_b200_table_selects_and_executes():
 
 
 @pytest.mark.parametrize("n, tiles", [(16, (16,)), (32, (32,)), (64, (64,)), (128, (128,)), (256, (256,)),
-                                      (1024, (1024,)), (4096, (4096,)), (8192, (256, 512)),
+                                      (512, (512,)), (1024, (1024,)), (2048, (2048,)), (4096, (4096,)),
+                                      (8192, (256, 512)),
                                       (65536, (256,)), (1 << 18, (64, 512))])
 def test_tma_passes_odd_batches(n, tiles):
-    """The bulk-copy row pass (partial last tiles when B is not a multiple of
-    the rows per tile; padded per-row copies below 256 points) and the TMA
+    """The row-pair kernel and the bulk-copy row pass (partial last tiles when
+    B is not a multiple of the rows per tile; padded per-row copies below 256
+    points and in the row-pair stages of 256 and 1024 points) and the TMA
     column pass (every tail pass, strided local groups), both directions,
     forward and ortho inverse."""
     rng = np.random.default_rng(n)
