@@ -493,8 +493,9 @@ static cudaError_t launch_fused_t(const float2* in, float2* out, const FusedArgs
 // 2.98 ms -- the larger rings no longer stay in L2.  After the kernel got
 // faster (shared-memory accesses as such, sleeping waits) the optimum moved
 // for long runs: N = 2^16, B = 8192 (4 GiB) takes 2.29 ms at 1280/1280 (a
-// 40 MiB ring) against 2.36 ms at 1536/1536 (1152/1152 2.33, 1280/1024 2.31,
-// 1024/1024 2.40, 1792/1792 2.53), while a 128 MiB batch (B N = 2^24) stays
+// 40 MiB ring) against 2.36 ms at 1536/1536 (1408/1408 2.30, 1152/1152 2.33,
+// 1280/1024 2.31, 1280/1536 2.34, 1152/1280 2.34, 1024/1024 2.40, 1792/1792
+// 2.53), while a 128 MiB batch (B N = 2^24) stays
 // faster at 1536/1536 (N = 2^13: 99-102 against 105 us; N = 2^16: 97 against
 // 103 us).  Batches of 2^26 points (512 MiB) or more use the smaller ring.
 constexpr int kLagTickets = 1536, kSlackTickets = 1536;
